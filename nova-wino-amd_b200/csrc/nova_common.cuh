@@ -1,0 +1,93 @@
+// Shared definitions for the NOVA F(6,3) Winograd library (sm_100a).
+//
+// NOVA interpolation points {0, +-3/5, +-1, +-7/6, inf}; m = 6 outputs, r = 3 taps,
+// tile n = 8.  The transform constants are the reference tables
+// (Jayluci4/nova-wino-amd csrc/nova_winograd.hip:68-97).  A and B are used at the
+// precision the reference computes with: the reference uploads them as __half
+// (csrc/nova_winograd.hip:103-131), so every A/B constant below is the FP16
+// rounding of the table entry written as an exact hex-float.  G stays FP32, as in
+// the reference.  The symmetric point pairs (+-p) make each 1-D transform an
+// even/odd butterfly, which is how the helpers below evaluate it.
+#pragma once
+
+#include <cuda_fp16.h>
+#include <cstdint>
+
+namespace nova {
+
+// ---- B (input transform V = B^T d B), FP16-rounded table entries ----------
+constexpr float kB049  = 0x1.f5cp-2f;   // 0.49
+constexpr float kB2211 = 0x1.1b0p+1f;   // 2.2111111111
+constexpr float kB2721 = 0x1.5c4p+1f;   // 2.7211111111
+constexpr float kB1361 = 0x1.5c8p+0f;   // 1.3611111111
+constexpr float kB2361 = 0x1.2e4p+1f;   // 2.3611111111
+constexpr float kB0817 = 0x1.a24p-1f;   // 0.8166666667
+constexpr float kB1417 = 0x1.6acp+0f;   // 1.4166666667
+constexpr float kB06   = 0x1.334p-1f;   // 0.6
+constexpr float kB1721 = 0x1.b88p+0f;   // 1.7211111111
+constexpr float kB036  = 0x1.70cp-2f;   // 0.36
+constexpr float kB1360 = 0x1.5c4p+0f;   // 1.36
+constexpr float kB042  = 0x1.ae0p-2f;   // 0.42
+constexpr float kB1587 = 0x1.964p+0f;   // 1.5866666667
+constexpr float kB1167 = 0x1.2acp+0f;   // 1.1666666667
+
+// ---- A (output transform Y = A M A^T), FP16-rounded table entries ---------
+constexpr float kA06    = 0x1.334p-1f;  // 0.6
+constexpr float kA1167  = 0x1.2acp+0f;  // 1.1666666667
+constexpr float kA036   = 0x1.70cp-2f;  // 0.36
+constexpr float kA1361  = 0x1.5c8p+0f;  // 1.3611111111
+constexpr float kA0216  = 0x1.ba4p-3f;  // 0.216
+constexpr float kA1588  = 0x1.968p+0f;  // 1.5879629630
+constexpr float kA01296 = 0x1.098p-3f;  // 0.1296
+constexpr float kA1853  = 0x1.da4p+0f;  // 1.8526234568
+constexpr float kA00778 = 0x1.3e8p-4f;  // 0.07776
+constexpr float kA2161  = 0x1.14cp+1f;  // 2.1613940329
+
+// ---- G (filter transform U = G w G^T), FP32 as in the reference -----------
+__host__ __device__ constexpr float kG(int i, int j) {
+  constexpr float g[8][3] = {
+      {-2.0408163265f, 0.0000000000f, 0.0000000000f},
+      {2.1677302997f, 1.3006381798f, 0.7803829079f},
+      {2.1677302997f, -1.3006381798f, 0.7803829079f},
+      {-2.1634615385f, -2.1634615385f, -2.1634615385f},
+      {-2.1634615385f, 2.1634615385f, -2.1634615385f},
+      {1.0161394021f, 1.1854959691f, 1.3830786306f},
+      {1.0161394021f, -1.1854959691f, 1.3830786306f},
+      {0.0000000000f, 0.0000000000f, 1.0000000000f}};
+  return g[i][j];
+}
+
+// f[r] = sum_i B[i][r] v[i]  (one 8-point input-transform pass).
+// Column r of B: r=0 (-.49,0,2.21,0,-2.72,0,1,0); r=1/2 = E1 +- O1; r=3/4 =
+// E2 +- O2; r=5/6 = E3 +- O3; r=7 (0,-.49,0,2.21,0,-2.72,0,1).
+__device__ __forceinline__ void bt_1d(const float v[8], float f[8]) {
+  const float e1 = fmaf(kB1361, v[2], fmaf(-kB2361, v[4], v[6]));
+  const float o1 = fmaf(kB0817, v[1], fmaf(-kB1417, v[3], kB06 * v[5]));
+  const float e2 = fmaf(kB049, v[2], fmaf(-kB1721, v[4], v[6]));
+  const float o2 = fmaf(kB049, v[1], fmaf(-kB1721, v[3], v[5]));
+  const float e3 = fmaf(kB036, v[2], fmaf(-kB1360, v[4], v[6]));
+  const float o3 = fmaf(kB042, v[1], fmaf(-kB1587, v[3], kB1167 * v[5]));
+  f[0] = fmaf(-kB049, v[0], fmaf(kB2211, v[2], fmaf(-kB2721, v[4], v[6])));
+  f[1] = e1 + o1;
+  f[2] = e1 - o1;
+  f[3] = e2 + o2;
+  f[4] = e2 - o2;
+  f[5] = e3 + o3;
+  f[6] = e3 - o3;
+  f[7] = fmaf(-kB049, v[1], fmaf(kB2211, v[3], fmaf(-kB2721, v[5], v[7])));
+}
+
+// g[i] = sum_p A[i][p] m[p]  (one 8 -> 6 output-transform pass).
+__device__ __forceinline__ void a_1d(const float m[8], float g[6]) {
+  const float sa = m[1] + m[2], da = m[1] - m[2];
+  const float sb = m[3] + m[4], db = m[3] - m[4];
+  const float sc = m[5] + m[6], dc = m[5] - m[6];
+  g[0] = m[0] + sa + sb + sc;
+  g[1] = fmaf(kA06, da, fmaf(kA1167, dc, db));
+  g[2] = fmaf(kA036, sa, fmaf(kA1361, sc, sb));
+  g[3] = fmaf(kA0216, da, fmaf(kA1588, dc, db));
+  g[4] = fmaf(kA01296, sa, fmaf(kA1853, sc, sb));
+  g[5] = fmaf(kA00778, da, fmaf(kA2161, dc, db)) + m[7];
+}
+
+}  // namespace nova

@@ -1,0 +1,445 @@
+// The 64 per-frequency Winograd GEMMs on the 5th-generation tensor cores.
+//
+//   M[pos][bp][k] = sum_c V[pos][bp][c] * U[pos][k][c]       pos = 0..63
+//
+// This replaces the reference's rocBLAS gemm_strided_batched_ex call
+// (Jayluci4/nova-wino-amd csrc/nova_winograd.hip:534-548: FP16 in, FP32
+// compute, FP16 out, batch 64).  Design:
+//
+// * Persistent kernel, one CTA per SM, tiles enumerated pos-major, then bp tile,
+//   then k tile, so CTAs running at the same time share U[pos] and V tiles in L2.
+// * Tile = 128 bp rows (MMA M, TMEM lanes) x BN output channels (MMA N <= 256)
+//   x 64 input channels per pipeline stage (one 128-byte SWIZZLE_128B row).
+// * Warp 0: TMA producer (cp.async.bulk.tensor.3d, no multicast).  Warp 1: TMEM
+//   allocation and the single-thread tcgen05.mma issuer.  Warps 2-5: epilogue
+//   (tcgen05.ld -> FP16 -> global).  The accumulator is double buffered in TMEM
+//   (2 x BN columns) so the epilogue of tile i overlaps the MMAs of tile i+1.
+// * Every mbarrier wait is bounded (globaltimer); on expiry the kernel records a
+//   status code in device memory, stops issuing work and returns.
+#include <cstdio>
+#include <cstring>
+
+#include "nova_internal.h"
+
+namespace nova {
+namespace tc {
+
+constexpr int kBM = 128;        // bp rows per tile
+constexpr int kBK = 64;         // input channels per stage (128 B of FP16)
+constexpr int kUmmaK = 16;      // K of one kind::f16 MMA
+constexpr int kMaxStages = 8;
+constexpr int kThreads = 192;   // 6 warps
+constexpr int kTmemCols = 512;
+constexpr unsigned long long kWaitLimitNs = 2000000000ull;  // 2 s per wait
+constexpr int kSmemLimit = 227 * 1024;
+
+struct Params {
+  __half* M;
+  long long BP;
+  int C, K, BN;
+  int n_bp_tiles, n_k_tiles, n_cblk;
+  long long total_tiles;
+  int stages;
+  int* status;
+};
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ uint64_t globaltimer() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes)
+               : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Bounded wait.  Returns false (and raises the CTA abort flag and the device
+// status) when the phase did not complete within kWaitLimitNs or another role
+// already aborted.
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort_flag,
+                                          int* status, int code) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = globaltimer();
+  for (uint32_t i = 1;; ++i) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if ((i & 255u) == 0) {
+      if (*abort_flag) return false;
+      if (globaltimer() - t0 > kWaitLimitNs) {
+        *abort_flag = 1;
+        atomicCAS(status, 0, code);
+        return false;
+      }
+    }
+  }
+}
+
+__device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap* map, int c0, int c1,
+                                            int c2, uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3, %4}], [%5];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(bar)
+      : "memory");
+}
+
+// Shared-memory matrix descriptor: K-major operand, SWIZZLE_128B, 8-row atoms
+// 1024 B apart (SBO), descriptor version 1 (sm_100).
+__device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t addr) {
+  return (uint64_t)((addr & 0x3FFFFu) >> 4) | (1ull << 16) | (64ull << 32) | (1ull << 46) |
+         (2ull << 61);
+}
+
+__device__ __forceinline__ void umma_f16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc,
+                                         uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+__device__ __forceinline__ void umma_commit(uint32_t bar) {
+  asm volatile(
+      "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar)
+      : "memory");
+}
+
+__device__ __forceinline__ void tc_fence_before() {
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_after() {
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+      "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
+      "%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+        "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]),
+        "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]),
+        "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ uint32_t pack_half2(uint32_t a, uint32_t b) {
+  __half2 h = __floats2half2_rn(__uint_as_float(a), __uint_as_float(b));
+  return *reinterpret_cast<uint32_t*>(&h);
+}
+
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_tc_kernel(const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmU,
+                   const Params p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~uintptr_t(1023));
+  const int S = p.stages;
+  const uint32_t a_bytes = kBM * kBK * 2;
+  const uint32_t b_bytes = (uint32_t)p.BN * kBK * 2;
+  const uint32_t stage_bytes = a_bytes + b_bytes;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(base + (size_t)S * stage_bytes);
+  uint64_t* full = bars;
+  uint64_t* empty = bars + kMaxStages;
+  uint64_t* tfull = bars + 2 * kMaxStages;
+  uint64_t* tempty = tfull + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S; ++s) {
+      mbar_init(smem_u32(&full[s]), 1);
+      mbar_init(smem_u32(&empty[s]), 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(smem_u32(&tfull[a]), 1);
+      mbar_init(smem_u32(&tempty[a]), 128);
+    }
+    *abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     smem_u32(tmem_slot)),
+                 "r"(kTmemCols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+  const long long tiles_per_pos = (long long)p.n_bp_tiles * p.n_k_tiles;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ---------------- TMA producer ----------------
+      int s = 0;
+      uint32_t ph = 0;
+      bool ok = true;
+      for (long long t = blockIdx.x; t < p.total_tiles && ok; t += gridDim.x) {
+        const int pos = (int)(t / tiles_per_pos);
+        const long long rem = t % tiles_per_pos;
+        const int bpt = (int)(rem / p.n_k_tiles);
+        const int kt = (int)(rem % p.n_k_tiles);
+        for (int cb = 0; cb < p.n_cblk; ++cb) {
+          if (!mbar_wait(smem_u32(&empty[s]), ph ^ 1u, abort_flag, p.status, kDevTimeoutProducer)) {
+            ok = false;
+            break;
+          }
+          const uint32_t sa = smem_u32(base + (size_t)s * stage_bytes);
+          const uint32_t fb = smem_u32(&full[s]);
+          mbar_expect_tx(fb, stage_bytes);
+          tma_load_3d(sa, &tmV, cb * kBK, bpt * kBM, pos, fb);
+          tma_load_3d(sa + a_bytes, &tmU, cb * kBK, kt * p.BN, pos, fb);
+          if (++s == S) {
+            s = 0;
+            ph ^= 1u;
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // ---------------- MMA issuer ----------------
+      const uint32_t idesc =
+          (1u << 4) | ((uint32_t)(p.BN >> 3) << 17) | ((uint32_t)(kBM >> 4) << 24);
+      int s = 0;
+      uint32_t ph = 0;
+      uint32_t it = 0;
+      bool ok = true;
+      for (long long t = blockIdx.x; t < p.total_tiles && ok; t += gridDim.x, ++it) {
+        const uint32_t acc = it & 1u;
+        const uint32_t aph = (it >> 1) & 1u;
+        if (!mbar_wait(smem_u32(&tempty[acc]), aph ^ 1u, abort_flag, p.status, kDevTimeoutMma))
+          break;
+        tc_fence_after();
+        const uint32_t dcol = tmem_base + acc * (uint32_t)p.BN;
+        for (int cb = 0; cb < p.n_cblk; ++cb) {
+          if (!mbar_wait(smem_u32(&full[s]), ph, abort_flag, p.status, kDevTimeoutMma)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t sa = smem_u32(base + (size_t)s * stage_bytes);
+          const uint64_t ad = smem_desc_sw128(sa);
+          const uint64_t bd = smem_desc_sw128(sa + a_bytes);
+#pragma unroll
+          for (int k = 0; k < kBK / kUmmaK; ++k) {
+            // +32 bytes along K inside the swizzled 128-byte row = +2 in the
+            // descriptor's 16-byte address units.
+            umma_f16(dcol, ad + 2ull * k, bd + 2ull * k, idesc, (cb | k) != 0);
+          }
+          umma_commit(smem_u32(&empty[s]));
+          if (++s == S) {
+            s = 0;
+            ph ^= 1u;
+          }
+        }
+        if (ok) umma_commit(smem_u32(&tfull[acc]));
+      }
+    }
+  } else {
+    // ---------------- Epilogue: warps 2..5 ----------------
+    const int q = warp & 3;  // TMEM lane quarter this warp may access
+    const int row = q * 32 + lane;
+    uint32_t it = 0;
+    for (long long t = blockIdx.x; t < p.total_tiles; t += gridDim.x, ++it) {
+      const int pos = (int)(t / tiles_per_pos);
+      const long long rem = t % tiles_per_pos;
+      const int bpt = (int)(rem / p.n_k_tiles);
+      const int kt = (int)(rem % p.n_k_tiles);
+      const uint32_t acc = it & 1u;
+      const uint32_t aph = (it >> 1) & 1u;
+      if (!mbar_wait(smem_u32(&tfull[acc]), aph, abort_flag, p.status, kDevTimeoutEpilogue)) break;
+      tc_fence_after();
+      const long long bp = (long long)bpt * kBM + row;
+      __half* out = p.M + ((long long)pos * p.BP + bp) * p.K + (long long)kt * p.BN;
+      const uint32_t taddr = tmem_base + ((uint32_t)(q * 32) << 16) + acc * (uint32_t)p.BN;
+      for (int j = 0; j < p.BN / 32; ++j) {
+        uint32_t r[32];
+        tmem_ld32(taddr + j * 32, r);
+        if (bp < p.BP) {
+          uint4* o = reinterpret_cast<uint4*>(out + j * 32);
+#pragma unroll
+          for (int v = 0; v < 4; ++v) {
+            uint4 w;
+            w.x = pack_half2(r[8 * v + 0], r[8 * v + 1]);
+            w.y = pack_half2(r[8 * v + 2], r[8 * v + 3]);
+            w.z = pack_half2(r[8 * v + 4], r[8 * v + 5]);
+            w.w = pack_half2(r[8 * v + 6], r[8 * v + 7]);
+            o[v] = w;
+          }
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(smem_u32(&tempty[acc]));
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base),
+                 "r"(kTmemCols)
+                 : "memory");
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Host side.
+// ---------------------------------------------------------------------------
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                   const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                   const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                   CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeTiledFn get_encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static bool tried = false;
+  if (!tried) {
+    tried = true;
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  }
+  return fn;
+}
+
+// 3-D FP16 map over [64][rows][C] (C fastest), box {64, box_rows, 1}, SWIZZLE_128B.
+static bool encode_operand_map(CUtensorMap* map, const void* ptr, int C, long long rows,
+                               int box_rows) {
+  EncodeTiledFn fn = get_encode_fn();
+  if (!fn) return false;
+  cuuint64_t dims[3] = {(cuuint64_t)C, (cuuint64_t)rows, 64};
+  cuuint64_t strides[2] = {(cuuint64_t)C * 2, (cuuint64_t)C * 2 * (cuuint64_t)rows};
+  cuuint32_t box[3] = {(cuuint32_t)kBK, (cuuint32_t)box_rows, 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  return fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, const_cast<void*>(ptr), dims, strides, box,
+            estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+static int pick_bn(int K) {
+  for (int bn = 256; bn >= 16; bn -= 16)
+    if (K % bn == 0) return bn;
+  return 0;
+}
+
+}  // namespace tc
+
+bool tc_gemm_supported(int C, int K) {
+  return C > 0 && K > 0 && (C % 8) == 0 && (K % 16) == 0 && tc::pick_bn(K) > 0;
+}
+
+cudaError_t tc_gemm_plan(TcGemmPlan* plan, const __half* U, int K, int C, const char** why) {
+  plan->valid = false;
+  if (!tc_gemm_supported(C, K)) {
+    *why = "shape not supported by the tensor-core GEMM";
+    return cudaErrorInvalidValue;
+  }
+  if (reinterpret_cast<uintptr_t>(U) % 16) {
+    *why = "U not 16-byte aligned";
+    return cudaErrorInvalidValue;
+  }
+  plan->BN = tc::pick_bn(K);
+  plan->K = K;
+  plan->C = C;
+  if (!tc::encode_operand_map(&plan->tmU, U, C, K, plan->BN)) {
+    *why = "cuTensorMapEncodeTiled failed for U";
+    return cudaErrorInvalidValue;
+  }
+  plan->valid = true;
+  return cudaSuccess;
+}
+
+cudaError_t tc_gemm_run(const TcGemmPlan& plan, const __half* V, __half* M, long long BP,
+                        int* dev_status, int num_sms, cudaStream_t s, const char** why) {
+  if (!plan.valid) {
+    *why = "tensor-core GEMM plan not built";
+    return cudaErrorInvalidValue;
+  }
+  if (BP <= 0) return cudaSuccess;
+  if (reinterpret_cast<uintptr_t>(V) % 16 || reinterpret_cast<uintptr_t>(M) % 16) {
+    *why = "V/M workspace not 16-byte aligned";
+    return cudaErrorInvalidValue;
+  }
+  CUtensorMap tmV;
+  if (!tc::encode_operand_map(&tmV, V, plan.C, BP, tc::kBM)) {
+    *why = "cuTensorMapEncodeTiled failed for V";
+    return cudaErrorInvalidValue;
+  }
+  tc::Params p;
+  p.M = M;
+  p.BP = BP;
+  p.C = plan.C;
+  p.K = plan.K;
+  p.BN = plan.BN;
+  p.n_bp_tiles = (int)((BP + tc::kBM - 1) / tc::kBM);
+  p.n_k_tiles = plan.K / plan.BN;
+  p.n_cblk = (plan.C + tc::kBK - 1) / tc::kBK;
+  p.total_tiles = 64ll * p.n_bp_tiles * p.n_k_tiles;
+  p.status = dev_status;
+  const int stage_bytes = tc::kBM * tc::kBK * 2 + plan.BN * tc::kBK * 2;
+  const int overhead = 1024 + 256;
+  p.stages = (tc::kSmemLimit - overhead) / stage_bytes;
+  if (p.stages > tc::kMaxStages) p.stages = tc::kMaxStages;
+  const int smem = overhead + p.stages * stage_bytes;
+  // The shared-memory opt-in is a per-device function attribute.
+  static bool configured[64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64 || !configured[dev]) {
+    cudaError_t e = cudaFuncSetAttribute(tc::gemm_tc_kernel,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         tc::kSmemLimit);
+    if (e != cudaSuccess) {
+      *why = "cudaFuncSetAttribute(MaxDynamicSharedMemorySize) failed";
+      return e;
+    }
+    if (dev >= 0 && dev < 64) configured[dev] = true;
+  }
+  long long grid = p.total_tiles < num_sms ? p.total_tiles : num_sms;
+  tc::gemm_tc_kernel<<<(unsigned)grid, tc::kThreads, smem, s>>>(tmV, plan.tmU, p);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) *why = "tensor-core GEMM launch failed";
+  return e;
+}
+
+}  // namespace nova

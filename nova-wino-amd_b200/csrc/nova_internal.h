@@ -1,0 +1,45 @@
+// Internal declarations shared by the library's translation units.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include "nova_common.cuh"
+
+namespace nova {
+
+// Device-side status codes written by kernels whose waits are bounded.
+enum DeviceStatus : int {
+  kDevOk = 0,
+  kDevTimeoutProducer = 1,  // TMA producer gave up waiting for a free stage
+  kDevTimeoutMma = 2,       // MMA issuer gave up waiting for operands / accumulator
+  kDevTimeoutEpilogue = 3,  // epilogue gave up waiting for an accumulator
+};
+
+cudaError_t launch_filter_transform(const float* w, __half* U, int K, int C, bool ref_layout,
+                                    cudaStream_t s);
+cudaError_t launch_input_transform(const __half* x, __half* V, int B, int C, int H, int W,
+                                   int pad, int nh, int nw, long long BP, cudaStream_t s);
+cudaError_t launch_output_transform(const __half* M, __half* y, int B, int K, int H_out,
+                                    int W_out, int nh, int nw, long long BP, cudaStream_t s);
+cudaError_t launch_gemm_simt(const __half* V, const __half* U, __half* M, long long BP, int C,
+                             int K, cudaStream_t s);
+
+// Tensor-core (tcgen05 + TMA) batched GEMM.
+struct TcGemmPlan {
+  CUtensorMap tmU;  // U internal layout [64][K][C], box {64 c, BN k, 1}
+  int BN = 0;       // output channels per tile (MMA N)
+  int K = 0, C = 0;
+  bool valid = false;
+};
+
+// True when (C, K) is a shape the tcgen05 path takes.
+bool tc_gemm_supported(int C, int K);
+// Builds the weight-side tensor map for U (call when the weights change).
+cudaError_t tc_gemm_plan(TcGemmPlan* plan, const __half* U, int K, int C, const char** why);
+// M[pos][bp][k] = sum_c V[pos][bp][c] U[pos][k][c] on the tensor cores.
+cudaError_t tc_gemm_run(const TcGemmPlan& plan, const __half* V, __half* M, long long BP,
+                        int* dev_status, int num_sms, cudaStream_t s, const char** why);
+
+}  // namespace nova

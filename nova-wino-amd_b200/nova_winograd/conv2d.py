@@ -1,0 +1,303 @@
+"""NOVA Winograd Conv2d modules -- drop-in replacements for ``torch.nn.Conv2d``.
+
+Same classes, constructor arguments, attribute names and caching semantics as
+the reference (Jayluci4/nova-wino-amd ``nova_winograd/conv2d.py``):
+
+    NovaWinogradConv2d           inference module; the transformed filter U is
+                                 cached per ``weight._version`` and the V/M
+                                 workspace per input shape (conv2d.py:154-273)
+    NovaWinogradConv2dTrainable  native forward, FP32 PyTorch backward
+                                 (conv2d.py:280-293, :92-147)
+    NovaWinogradConv2dCompilable ``torch.library`` custom op
+                                 ``nova::winograd_conv2d`` so that
+                                 ``torch.compile(fullgraph=True)`` traces through
+                                 the native call (conv2d.py:25-85, :300-344)
+
+The native forward runs on the caller's current CUDA stream (the reference used
+the legacy default stream) and never synchronizes.
+"""
+
+import math
+
+import torch
+import torch.nn as nn
+import torch.nn.functional as F
+
+from nova_winograd.ops import (check, compute_tiling, create_handle, get_lib, ptr, stream_ptr,
+                               _ensure_lib)
+
+
+def _weight_grad(inp, weight, grad_out, padding):
+    """dL/dw of a 3x3 stride-1 conv in FP32 (reference conv2d.py:66-80 / :131-141)."""
+    return torch.nn.grad.conv2d_weight(inp.float(), weight.shape, grad_out.float(),
+                                       padding=padding)
+
+
+# ---------------------------------------------------------------------------
+# torch.compile custom op (reference conv2d.py:25-85)
+# ---------------------------------------------------------------------------
+
+_custom_op_registered = False
+
+
+def _register_custom_op():
+    global _custom_op_registered
+    if _custom_op_registered:
+        return
+    _custom_op_registered = True
+
+    @torch.library.custom_op("nova::winograd_conv2d", mutates_args=())
+    def nova_winograd_conv2d(input: torch.Tensor, weight: torch.Tensor,
+                             padding: int) -> torch.Tensor:
+        lib = get_lib()
+        x = input.half().contiguous() if input.dtype != torch.float16 else input.contiguous()
+        w = weight.float().contiguous() if weight.dtype != torch.float32 else weight.contiguous()
+        B, C, H, W = x.shape
+        K = w.shape[0]
+        _, _, H_out, W_out = compute_tiling(H, W, padding)
+        output = torch.empty(B, K, H_out, W_out, dtype=torch.float16, device=x.device)
+        with torch.cuda.device(x.device):
+            s = stream_ptr()
+            handle = create_handle(x.device)
+            try:
+                check(lib.nova_set_weights_v2(handle, ptr(w), K, C, s), "nova_set_weights")
+                check(lib.nova_forward_v2(handle, ptr(x), ptr(output), B, H, W, padding, s),
+                      "nova_forward")
+                # The handle owns U and the workspace; finish before it is freed.
+                torch.cuda.current_stream().synchronize()
+            finally:
+                lib.nova_destroy(handle)
+        return output
+
+    @nova_winograd_conv2d.register_fake
+    def _(input, weight, padding):
+        B, C, H, W = input.shape
+        K = weight.shape[0]
+        return input.new_empty(B, K, H + 2 * padding - 2, W + 2 * padding - 2,
+                               dtype=torch.float16)
+
+    def _setup_context(ctx, inputs, output):
+        input, weight, padding = inputs
+        ctx.save_for_backward(input, weight)
+        ctx.padding = padding
+
+    def _backward(ctx, grad_output):
+        input, weight = ctx.saved_tensors
+        go = grad_output.contiguous()
+        grad_input = F.conv_transpose2d(go.float(), weight.float(),
+                                        padding=ctx.padding).to(input.dtype)
+        grad_weight = _weight_grad(input, weight, go, ctx.padding).to(weight.dtype)
+        return grad_input, grad_weight, None
+
+    nova_winograd_conv2d.register_autograd(_backward, setup_context=_setup_context)
+
+
+# ---------------------------------------------------------------------------
+# Autograd function: native forward, FP32 backward (reference conv2d.py:92-147)
+# ---------------------------------------------------------------------------
+
+class NovaWinogradFunction(torch.autograd.Function):
+
+    @staticmethod
+    def forward(ctx, input, weight, bias, padding, handle_holder):
+        ctx.save_for_backward(input, weight, bias)
+        ctx.padding = padding
+        x = input.half().contiguous() if input.dtype != torch.float16 else input.contiguous()
+        return handle_holder._native_forward(x, bias)
+
+    @staticmethod
+    def backward(ctx, grad_output):
+        input, weight, bias = ctx.saved_tensors
+        grad_input = grad_weight = grad_bias = None
+        go = grad_output.contiguous()
+        if ctx.needs_input_grad[0]:
+            grad_input = F.conv_transpose2d(go.float(), weight.float(),
+                                            padding=ctx.padding).to(input.dtype)
+        if ctx.needs_input_grad[1]:
+            grad_weight = _weight_grad(input, weight, go, ctx.padding).to(weight.dtype)
+        if bias is not None and ctx.needs_input_grad[2]:
+            grad_bias = go.float().sum(dim=(0, 2, 3)).to(bias.dtype)
+        return grad_input, grad_weight, grad_bias, None, None
+
+
+# ---------------------------------------------------------------------------
+# Inference module (reference conv2d.py:154-273)
+# ---------------------------------------------------------------------------
+
+class NovaWinogradConv2d(nn.Module):
+    """Drop-in replacement for nn.Conv2d (3x3, stride 1) using NOVA F(6,3).
+
+    Input must be float16 and contiguous.  Weights are stored in float32 and
+    transformed on first use and again whenever ``weight._version`` changes.
+    """
+
+    def __init__(self, in_channels, out_channels, kernel_size=3, padding=1, bias=False):
+        super().__init__()
+        if kernel_size not in (3, (3, 3)):
+            raise ValueError("Only 3x3 kernels supported")
+        self.in_channels = in_channels
+        self.out_channels = out_channels
+        self.padding = padding
+        self.weight = nn.Parameter(torch.empty(out_channels, in_channels, 3, 3))
+        nn.init.kaiming_uniform_(self.weight, a=math.sqrt(5))
+        if bias:
+            self.bias = nn.Parameter(torch.zeros(out_channels))
+        else:
+            self.register_parameter("bias", None)
+        self._handle = None
+        self._handle_device = None
+        self._weight_version = -1
+        self._weight_ptr = None
+        self._V_gemm = None
+        self._M_gemm = None
+        self._last_config = None
+
+    def _ensure_handle(self):
+        """Create the native context and refresh U when the weights changed."""
+        lib = get_lib()
+        dev = self.weight.device
+        if self._handle is not None and self._handle_device != dev:
+            lib.nova_destroy(self._handle)
+            self._handle = None
+        if self._handle is None:
+            self._handle = create_handle(dev)
+            self._handle_device = dev
+            self._weight_version = -1
+        version = self.weight._version
+        wptr = self.weight.data_ptr()
+        if version != self._weight_version or wptr != self._weight_ptr:
+            w = self.weight.data.float().contiguous()
+            check(lib.nova_set_weights_v2(self._handle, ptr(w), self.out_channels,
+                                          self.in_channels, stream_ptr()), "nova_set_weights")
+            # Keep the FP32 copy alive until the transform kernel has read it.
+            self._w_staging = w
+            self._weight_version = version
+            self._weight_ptr = wptr
+            self._V_gemm = None
+            self._M_gemm = None
+            self._last_config = None
+
+    def _ensure_workspace(self, batch, H, W):
+        """V/M workspace sized by the reference tiling (conv2d.py:205-220)."""
+        nh, nw, H_out, W_out = compute_tiling(H, W, self.padding)
+        BP = batch * nh * nw
+        config = (batch, H, W, self.padding, nh, nw, self.weight.device)
+        if self._last_config != config:
+            device = self.weight.device
+            self._V_gemm = torch.empty(64, self.in_channels, BP, dtype=torch.float16, device=device)
+            self._M_gemm = torch.empty(64, self.out_channels, BP, dtype=torch.float16,
+                                       device=device)
+            self._last_config = config
+        return nh, nw, H_out, W_out
+
+    def _native_forward(self, x, bias):
+        _ensure_lib()
+        if not x.is_cuda:
+            raise ValueError("input must be a CUDA tensor")
+        B, C, H, W = x.shape
+        if C != self.in_channels:
+            raise ValueError(f"expected {self.in_channels} input channels, got {C}")
+        if x.device != self.weight.device:
+            raise ValueError("input and weight are on different devices")
+        with torch.cuda.device(x.device):
+            self._ensure_handle()
+            nh, nw, H_out, W_out = self._ensure_workspace(B, H, W)
+            output = torch.empty(B, self.out_channels, H_out, W_out, dtype=torch.float16,
+                                 device=x.device)
+            check(get_lib().nova_forward_workspace_v2(
+                self._handle, ptr(x), ptr(output), ptr(self._V_gemm), ptr(self._M_gemm),
+                B, H, W, self.padding, nh, nw, stream_ptr()), "nova_forward_workspace")
+        if bias is not None:
+            output = output + bias.half().view(1, -1, 1, 1)
+        return output
+
+    def forward(self, x):
+        if x.dtype != torch.float16:
+            raise TypeError(f"Input must be float16, got {x.dtype}")
+        if not x.is_contiguous():
+            raise ValueError("Input must be contiguous")
+        return self._native_forward(x, self.bias)
+
+    def __del__(self):
+        try:
+            if self._handle is not None:
+                get_lib().nova_destroy(self._handle)
+                self._handle = None
+        except Exception:
+            pass
+
+    @classmethod
+    def from_conv2d(cls, conv):
+        """Create from an existing nn.Conv2d (reference conv2d.py:253-267)."""
+        if conv.kernel_size != (3, 3):
+            raise ValueError("Only 3x3 kernels supported")
+        if conv.stride != (1, 1):
+            raise ValueError("Only stride=1 supported")
+        if isinstance(conv.padding, str) or conv.padding[0] != conv.padding[1]:
+            raise ValueError("Only symmetric integer padding supported")
+        nova_conv = cls(conv.in_channels, conv.out_channels, kernel_size=3,
+                        padding=conv.padding[0], bias=conv.bias is not None)
+        nova_conv = nova_conv.to(conv.weight.device)
+        nova_conv.weight.data.copy_(conv.weight.data.float())
+        if conv.bias is not None:
+            nova_conv.bias.data.copy_(conv.bias.data.float())
+        return nova_conv
+
+    def extra_repr(self):
+        return (f"in_channels={self.in_channels}, out_channels={self.out_channels}, "
+                f"kernel_size=3, padding={self.padding}, tile=F(6,3), points=NOVA")
+
+
+class NovaWinogradConv2dTrainable(NovaWinogradConv2d):
+    """NOVA conv with a backward pass: native forward, FP32 PyTorch backward."""
+
+    def forward(self, x):
+        if not x.is_contiguous():
+            x = x.contiguous()
+        if x.dtype != torch.float16:
+            x = x.half()
+        if x.shape[1] != self.in_channels:
+            raise ValueError(f"expected {self.in_channels} input channels, got {x.shape[1]}")
+        return NovaWinogradFunction.apply(x, self.weight, self.bias, self.padding, self)
+
+
+class NovaWinogradConv2dCompilable(nn.Module):
+    """NOVA conv usable under ``torch.compile(fullgraph=True)`` via a custom op."""
+
+    def __init__(self, in_channels, out_channels, kernel_size=3, padding=1, bias=False):
+        super().__init__()
+        if kernel_size not in (3, (3, 3)):
+            raise ValueError("Only 3x3 kernels supported")
+        _register_custom_op()
+        self.in_channels = in_channels
+        self.out_channels = out_channels
+        self.padding = padding
+        self.weight = nn.Parameter(torch.empty(out_channels, in_channels, 3, 3))
+        nn.init.kaiming_uniform_(self.weight, a=math.sqrt(5))
+        if bias:
+            self.bias = nn.Parameter(torch.zeros(out_channels))
+        else:
+            self.register_parameter("bias", None)
+
+    def forward(self, x):
+        out = torch.ops.nova.winograd_conv2d(x, self.weight, self.padding)
+        if self.bias is not None:
+            out = out + self.bias.half().view(1, -1, 1, 1)
+        return out
+
+    @classmethod
+    def from_conv2d(cls, conv):
+        if conv.kernel_size != (3, 3) or conv.stride != (1, 1):
+            raise ValueError("Only 3x3 stride-1 convolutions supported")
+        nova = cls(conv.in_channels, conv.out_channels, padding=conv.padding[0],
+                   bias=conv.bias is not None)
+        nova = nova.to(conv.weight.device)
+        nova.weight.data.copy_(conv.weight.data.float())
+        if conv.bias is not None:
+            nova.bias.data.copy_(conv.bias.data.float())
+        return nova
+
+    def extra_repr(self):
+        return (f"in_channels={self.in_channels}, out_channels={self.out_channels}, "
+                f"kernel_size=3, padding={self.padding}, tile=F(6,3), points=NOVA, "
+                f"compilable=True")

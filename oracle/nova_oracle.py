@@ -1,0 +1,260 @@
+"""CPU oracle for the NOVA F(6,3) Winograd 3x3 stride-1 convolution forward.
+
+TEST INFRASTRUCTURE ONLY.  This module is the checker for the CUDA library in
+``nova-wino-amd_b200/``; it is imported by ``tests/``, by
+``__graft_entry__.smoke()`` and by the ``cpu_baseline`` / ``--impl reference``
+legs of ``bench.py``.  The product path never imports it, and there is no CPU
+fallback anywhere in the library.
+
+It restates, in numpy float32, the algorithm of the reference implementation
+(Jayluci4/nova-wino-amd, HIP + rocBLAS for MI300X):
+
+* transform matrices            ``csrc/nova_winograd.hip:68-97`` (points
+                                {0, +-3/5, +-1, +-7/6, inf}, ``:45``)
+* their FP16 upload             ``csrc/nova_winograd.hip:103-131`` (A and B are
+                                stored as ``__half``; G stays FP32)
+* tiling                        ``csrc/nova_winograd.hip:617-631``
+* filter transform              ``csrc/nova_winograd.hip:214-255`` (U = G w G^T
+                                in FP32, stored FP16 as ``U[pos][c][k]``)
+* input transform               ``csrc/nova_winograd.hip:338-392`` (V = B^T d B
+                                with fused zero padding, tile origin
+                                ``th*6-pad``, stored FP16 as ``V[pos][bp][c]``)
+* batched GEMM                  rocBLAS ``gemm_strided_batched_ex`` at
+                                ``csrc/nova_winograd.hip:534-548`` (64 GEMMs,
+                                FP16 in, FP32 accumulate, FP16 out ``M[pos][bp][k]``)
+* output transform              ``csrc/nova_winograd.hip:398-450`` (Y = A M A^T,
+                                bounds-checked NCHW store, FP16)
+
+Two modes:
+
+``"ref"``   FP32 arithmetic with the reference's storage roundings: FP16 A/B
+            constants, FP16 V, U, M and output.  This is the reference's
+            numerics; the CUDA path is compared against it.
+``"exact"`` FP32 everywhere, FP32 constants, no intermediate rounding.  The
+            error of "ref" against an FP64 direct convolution is the accuracy
+            bar (the CUDA path must be no worse than 1.1x of it).
+
+The GEMM arithmetic of the reference lives in rocBLAS (ROCm 6.3, not vendored);
+its published contract -- D = alpha*A*B + beta*C with FP32 compute and FP16
+result rounding to nearest -- is what ``gemm`` restates.
+"""
+
+from __future__ import annotations
+
+import numpy as np
+
+# ---------------------------------------------------------------------------
+# a1: NOVA transform matrices, csrc/nova_winograd.hip:68-97 (host tables).
+# ---------------------------------------------------------------------------
+
+NOVA_POINTS = (0.0, 3.0 / 5.0, -3.0 / 5.0, 1.0, -1.0, 7.0 / 6.0, -7.0 / 6.0)  # + infinity
+
+A_TABLE = np.array([
+    [1.0000000000, 1.0000000000, 1.0000000000, 1.0000000000, 1.0000000000, 1.0000000000, 1.0000000000, 0.0000000000],
+    [0.0000000000, 0.6000000000, -0.6000000000, 1.0000000000, -1.0000000000, 1.1666666667, -1.1666666667, 0.0000000000],
+    [0.0000000000, 0.3600000000, 0.3600000000, 1.0000000000, 1.0000000000, 1.3611111111, 1.3611111111, 0.0000000000],
+    [0.0000000000, 0.2160000000, -0.2160000000, 1.0000000000, -1.0000000000, 1.5879629630, -1.5879629630, 0.0000000000],
+    [0.0000000000, 0.1296000000, 0.1296000000, 1.0000000000, 1.0000000000, 1.8526234568, 1.8526234568, 0.0000000000],
+    [0.0000000000, 0.0777600000, -0.0777600000, 1.0000000000, -1.0000000000, 2.1613940329, -2.1613940329, 1.0000000000],
+])
+
+B_TABLE = np.array([
+    [-0.4900000000, 0.0, 0.0, 0.0, 0.0, 0.0, 0.0, 0.0],
+    [0.0, 0.8166666667, -0.8166666667, 0.4900000000, -0.4900000000, 0.4200000000, -0.4200000000, -0.4900000000],
+    [2.2111111111, 1.3611111111, 1.3611111111, 0.4900000000, 0.4900000000, 0.3600000000, 0.3600000000, 0.0],
+    [0.0, -1.4166666667, 1.4166666667, -1.7211111111, 1.7211111111, -1.5866666667, 1.5866666667, 2.2111111111],
+    [-2.7211111111, -2.3611111111, -2.3611111111, -1.7211111111, -1.7211111111, -1.3600000000, -1.3600000000, 0.0],
+    [0.0, 0.6000000000, -0.6000000000, 1.0000000000, -1.0000000000, 1.1666666667, -1.1666666667, -2.7211111111],
+    [1.0000000000, 1.0000000000, 1.0000000000, 1.0000000000, 1.0000000000, 1.0000000000, 1.0000000000, 0.0],
+    [0.0, 0.0, 0.0, 0.0, 0.0, 0.0, 0.0, 1.0000000000],
+])
+
+G_TABLE = np.array([
+    [-2.0408163265, 0.0000000000, 0.0000000000],
+    [2.1677302997, 1.3006381798, 0.7803829079],
+    [2.1677302997, -1.3006381798, 0.7803829079],
+    [-2.1634615385, -2.1634615385, -2.1634615385],
+    [-2.1634615385, 2.1634615385, -2.1634615385],
+    [1.0161394021, 1.1854959691, 1.3830786306],
+    [1.0161394021, -1.1854959691, 1.3830786306],
+    [0.0000000000, 0.0000000000, 1.0000000000],
+])
+
+M_OUT, R_FILT, N_TILE = 6, 3, 8
+
+
+def matrices(mode: str = "ref"):
+    """Return (A, B, G) as float32 in the precision the given mode computes with.
+
+    "ref": A and B go through float -> __half exactly as
+    ``upload_transform_matrices`` does (csrc/nova_winograd.hip:103-131); G stays FP32.
+    """
+    A = A_TABLE.astype(np.float32)
+    B = B_TABLE.astype(np.float32)
+    G = G_TABLE.astype(np.float32)
+    if mode == "ref":
+        A = A.astype(np.float16).astype(np.float32)
+        B = B.astype(np.float16).astype(np.float32)
+    elif mode != "exact":
+        raise ValueError(f"unknown oracle mode {mode!r}")
+    return A, B, G
+
+
+def cook_toom_residual() -> float:
+    """Max |error| of the 1-D F(6,3) identity  y = A [(G g) * (B^T d)]  in FP64.
+
+    Checks the reference tables against the definition of a Winograd minimal
+    filter: for any 8-sample signal d and 3-tap filter g the 6 outputs equal
+    the valid correlation.
+    """
+    rng = np.random.default_rng(0)
+    worst = 0.0
+    for _ in range(64):
+        d = rng.standard_normal(8)
+        g = rng.standard_normal(3)
+        y = A_TABLE @ ((G_TABLE @ g) * (B_TABLE.T @ d))
+        ref = np.array([d[i:i + 3] @ g for i in range(6)])
+        worst = max(worst, float(np.max(np.abs(y - ref))))
+    return worst
+
+
+# ---------------------------------------------------------------------------
+# a2: tiling, csrc/nova_winograd.hip:617-631 (also ops.py:128-144).
+# ---------------------------------------------------------------------------
+
+def compute_tiling(H: int, W: int, pad: int):
+    """(nh, nw, H_out, W_out) exactly as the reference computes them."""
+    m, n = M_OUT, N_TILE
+    H_out = H + 2 * pad - 2
+    W_out = W + 2 * pad - 2
+    H_pad = H_out + n - 1
+    W_pad = W_out + n - 1
+    H_pad += (m - (H_pad - n) % m) % m
+    W_pad += (m - (W_pad - n) % m) % m
+    return (H_pad - n) // m + 1, (W_pad - n) // m + 1, H_out, W_out
+
+
+def live_tiling(H: int, W: int, pad: int):
+    """(nh, nw): tiles that cover at least one output pixel, ceil(H_out/6)."""
+    H_out = H + 2 * pad - 2
+    W_out = W + 2 * pad - 2
+    return -(-H_out // M_OUT), -(-W_out // M_OUT)
+
+
+# ---------------------------------------------------------------------------
+# a3-a6: the three passes.
+# ---------------------------------------------------------------------------
+
+def _round(x: np.ndarray, mode: str) -> np.ndarray:
+    return x.astype(np.float16) if mode == "ref" else x.astype(np.float32)
+
+
+def filter_transform(w: np.ndarray, mode: str = "ref") -> np.ndarray:
+    """U in the reference GEMM layout [64][C][K] (k fastest).
+
+    csrc/nova_winograd.hip:214-255: U[pos][k][c] = (G w_kc G^T)[pos] in FP32,
+    written at ``pos*K*C + k + c*K`` and rounded to FP16.
+    """
+    _, _, G = matrices(mode)
+    K, C = w.shape[:2]
+    u = G @ w.astype(np.float32) @ G.T                       # [K, C, 8, 8]
+    u = u.transpose(2, 3, 1, 0).reshape(64, C, K)
+    return _round(np.ascontiguousarray(u), mode)
+
+
+def input_tiles(x: np.ndarray, nh: int, nw: int, pad: int) -> np.ndarray:
+    """Overlapping 8x8 windows at stride 6, origin (th*6-pad, tw*6-pad), zero padded.
+
+    Returns float32 [B, C, nh, nw, 8, 8]; csrc/nova_winograd.hip:358-370.
+    """
+    Bn, C, H, W = x.shape
+    Hp = (nh - 1) * 6 + 8
+    Wp = (nw - 1) * 6 + 8
+    xp = np.zeros((Bn, C, Hp, Wp), dtype=np.float32)
+    hs, ws = min(H, Hp - pad), min(W, Wp - pad)
+    xp[:, :, pad:pad + hs, pad:pad + ws] = x[:, :, :hs, :ws].astype(np.float32)
+    win = np.lib.stride_tricks.sliding_window_view(xp, (8, 8), axis=(2, 3))
+    return np.ascontiguousarray(win[:, :, ::6, ::6])
+
+
+def input_transform(x: np.ndarray, nh: int, nw: int, pad: int, mode: str = "ref") -> np.ndarray:
+    """V in the reference GEMM layout [64][B*P][C] (c fastest).
+
+    csrc/nova_winograd.hip:372-391: temp = B^T d, V = temp B, stored at
+    ``pos*C*BP + c + bp*C`` with bp = b*P + th*nw + tw.
+    """
+    _, Bm, _ = matrices(mode)
+    Bn, C = x.shape[:2]
+    d = input_tiles(x, nh, nw, pad)
+    v = Bm.T @ d @ Bm                                        # [B, C, nh, nw, 8, 8]
+    v = v.transpose(4, 5, 0, 2, 3, 1).reshape(64, Bn * nh * nw, C)
+    return _round(np.ascontiguousarray(v), mode)
+
+
+def gemm(U: np.ndarray, V: np.ndarray, mode: str = "ref") -> np.ndarray:
+    """M[pos][bp][k] = sum_c V[pos][bp][c] * U[pos][c][k], FP32 accumulate.
+
+    rocBLAS gemm_strided_batched_ex at csrc/nova_winograd.hip:534-548 (column
+    major M(KxBP) = U(KxC) V(CxBP), which is this row-major product).
+    """
+    m = np.matmul(V.astype(np.float32), U.astype(np.float32))
+    return _round(m, mode)
+
+
+def output_transform(M: np.ndarray, Bn: int, nh: int, nw: int, H_out: int, W_out: int,
+                     mode: str = "ref") -> np.ndarray:
+    """y NCHW [B, K, H_out, W_out] from M[64][B*P][K]; csrc/nova_winograd.hip:420-449."""
+    A, _, _ = matrices(mode)
+    K = M.shape[2]
+    m = M.astype(np.float32).reshape(8, 8, Bn, nh, nw, K).transpose(2, 5, 3, 4, 0, 1)
+    y = A @ m @ A.T                                          # [B, K, nh, nw, 6, 6]
+    y = _round(y, mode)
+    y = y.transpose(0, 1, 2, 4, 3, 5).reshape(Bn, K, nh * 6, nw * 6)
+    return np.ascontiguousarray(y[:, :, :H_out, :W_out])
+
+
+def nova_forward(x: np.ndarray, w: np.ndarray, pad: int = 1, mode: str = "ref",
+                 live_tiles_only: bool = True) -> np.ndarray:
+    """Whole NOVA forward on CPU.  ``x`` [B,C,H,W] (FP16 values), ``w`` [K,C,3,3] FP32.
+
+    Tiles beyond ceil(H_out/6) (the reference's over-tiling) lie entirely in the
+    padding and write nothing (csrc/nova_winograd.hip:446), so skipping them
+    changes no output value.
+    """
+    Bn, C, H, W = x.shape
+    nh, nw, H_out, W_out = compute_tiling(H, W, pad)
+    if live_tiles_only:
+        nh, nw = live_tiling(H, W, pad)
+    U = filter_transform(w, mode)
+    V = input_transform(x, nh, nw, pad, mode)
+    M = gemm(U, V, mode)
+    return output_transform(M, Bn, nh, nw, H_out, W_out, mode)
+
+
+# ---------------------------------------------------------------------------
+# FP64 direct convolution (the accuracy yardstick) and the error metric.
+# ---------------------------------------------------------------------------
+
+def direct_conv_fp64(x: np.ndarray, w: np.ndarray, pad: int = 1) -> np.ndarray:
+    Bn, C, H, W = x.shape
+    K = w.shape[0]
+    xp = np.zeros((Bn, C, H + 2 * pad, W + 2 * pad), dtype=np.float64)
+    xp[:, :, pad:pad + H, pad:pad + W] = x.astype(np.float64)
+    H_out, W_out = H + 2 * pad - 2, W + 2 * pad - 2
+    win = np.lib.stride_tricks.sliding_window_view(xp, (3, 3), axis=(2, 3))[:, :, :H_out, :W_out]
+    return np.einsum("bchwij,kcij->bkhw", win, w.astype(np.float64), optimize=True)
+
+
+def rel_l2(a: np.ndarray, ref: np.ndarray) -> float:
+    a = a.astype(np.float64)
+    ref = ref.astype(np.float64)
+    return float(np.linalg.norm((a - ref).ravel()) / np.linalg.norm(ref.ravel()))
+
+
+def synthetic_case(B: int, C: int, K: int, H: int, W: int, seed: int):
+    """Seeded inputs of the benchmark distributions: x ~ N(0,1) -> FP16,
+    w ~ Kaiming-normal (std sqrt(2/(9C))) FP32."""
+    rng = np.random.default_rng(seed)
+    x = rng.standard_normal((B, C, H, W), dtype=np.float32).astype(np.float16)
+    w = (rng.standard_normal((K, C, 3, 3), dtype=np.float32) * np.float32(np.sqrt(2.0 / (9 * C))))
+    return x, w.astype(np.float32)

@@ -1,0 +1,196 @@
+"""GPU tests of the Python surface, case for case the reference suite
+(Jayluci4/nova-wino-amd tests/test_correctness.py) with its thresholds, plus
+the stricter oracle bar where the reference compared only to FP32 conv."""
+
+import numpy as np
+import pytest
+import torch
+import torch.nn as nn
+import torch.nn.functional as F
+
+import nova_oracle as o
+from nova_winograd import (NovaWinogradConv2d, NovaWinogradConv2dCompilable,
+                           NovaWinogradConv2dTrainable, nova_forward, ops,
+                           replace_conv2d_with_nova)
+
+pytestmark = pytest.mark.gpu
+
+SHAPE_CONFIGS = [  # tests/test_correctness.py:38-47
+    (1, 64, 64, 56, 56, 1),
+    (1, 128, 128, 28, 28, 1),
+    (1, 256, 256, 14, 14, 1),
+    (1, 512, 512, 7, 7, 1),
+    (4, 64, 64, 56, 56, 1),
+    (8, 128, 256, 28, 28, 1),
+    (1, 3, 64, 224, 224, 1),
+    (2, 64, 64, 32, 32, 1),
+]
+
+
+@pytest.mark.parametrize("B,C,K,H,W,pad", SHAPE_CONFIGS)
+def test_basic_shapes(B, C, K, H, W, pad):
+    conv = NovaWinogradConv2d(C, K, kernel_size=3, padding=pad).cuda()
+    x = torch.randn(B, C, H, W, device="cuda", dtype=torch.float16)
+    out = conv(x)
+    assert out.shape == (B, K, H + 2 * pad - 2, W + 2 * pad - 2)
+    assert torch.isfinite(out).all()
+
+
+ACCURACY_CONFIGS = [  # tests/test_correctness.py:63-69
+    ("conv2_x", 1, 64, 64, 56, 56),
+    ("conv3_x", 1, 128, 128, 28, 28),
+    ("conv4_x", 1, 256, 256, 14, 14),
+    ("conv5_x", 1, 512, 512, 7, 7),
+    ("batch8", 8, 64, 64, 56, 56),
+]
+
+
+@pytest.mark.parametrize("name,B,C,K,H,W", ACCURACY_CONFIGS)
+def test_accuracy_vs_direct_conv(name, B, C, K, H, W):
+    conv_ref = nn.Conv2d(C, K, 3, padding=1, bias=False).cuda()
+    x = torch.randn(B, C, H, W, device="cuda")
+    with torch.no_grad():
+        ref = conv_ref(x)
+    out = nova_forward(x.half(), conv_ref.weight.data.float().contiguous(), padding=1)
+    rel_err = (torch.norm(out.float() - ref) / torch.norm(ref)).item()
+    assert rel_err < 0.06, f"{name}: rel_err={rel_err:.6f}"
+    assert torch.isfinite(out).all()
+
+
+NAN_CONFIGS = [  # tests/test_correctness.py:89-96
+    (1, 64, 64, 56, 56),
+    (1, 128, 128, 28, 28),
+    (1, 256, 256, 14, 14),
+    (1, 512, 512, 7, 7),
+    (8, 64, 128, 56, 56),
+    (4, 256, 512, 14, 14),
+]
+
+
+@pytest.mark.parametrize("B,C,K,H,W", NAN_CONFIGS)
+def test_zero_nan_inf(B, C, K, H, W):
+    x = torch.randn(B, C, H, W, device="cuda", dtype=torch.float16)
+    w = torch.randn(K, C, 3, 3, device="cuda", dtype=torch.float32) * 0.5
+    out = nova_forward(x, w, padding=1)
+    assert torch.isfinite(out).all()
+
+
+def test_weight_caching():
+    conv = NovaWinogradConv2d(64, 64, kernel_size=3, padding=1).cuda()
+    x = torch.randn(1, 64, 28, 28, device="cuda", dtype=torch.float16)
+    out1 = conv(x).clone()
+    out2 = conv(x).clone()
+    assert torch.equal(out1, out2)
+    with torch.no_grad():
+        conv.weight.add_(0.1)
+    out3 = conv(x).clone()
+    assert not torch.allclose(out1, out3, atol=1e-3)
+
+
+def test_from_conv2d():
+    std_conv = nn.Conv2d(64, 128, 3, padding=1, bias=True).cuda()
+    nova_conv = NovaWinogradConv2d.from_conv2d(std_conv).cuda()
+    assert torch.equal(std_conv.weight.data, nova_conv.weight.data)
+    assert torch.equal(std_conv.bias.data, nova_conv.bias.data)
+    x = torch.randn(1, 64, 28, 28, device="cuda")
+    with torch.no_grad():
+        ref = std_conv(x)
+        out = nova_conv(x.half())
+    assert (torch.norm(out.float() - ref) / torch.norm(ref)).item() < 0.06
+
+
+def test_backward_pass():
+    C, K = 32, 64
+    nova_conv = NovaWinogradConv2dTrainable(C, K, kernel_size=3, padding=1, bias=True).cuda()
+    ref_conv = nn.Conv2d(C, K, 3, padding=1, bias=True).cuda()
+    ref_conv.weight.data.copy_(nova_conv.weight.data)
+    ref_conv.bias.data.copy_(nova_conv.bias.data)
+    x = torch.randn(2, C, 14, 14, device="cuda", requires_grad=True)
+    ref_conv(x).sum().backward()
+    ref_gi = x.grad.clone()
+    x.grad = None
+    nova_conv(x).float().sum().backward()
+    gi_err = (torch.norm(x.grad - ref_gi) / torch.norm(ref_gi)).item()
+    gw_err = (torch.norm(nova_conv.weight.grad - ref_conv.weight.grad)
+              / torch.norm(ref_conv.weight.grad)).item()
+    assert gi_err < 0.10 and gw_err < 0.15
+    assert torch.allclose(nova_conv.bias.grad, ref_conv.bias.grad, rtol=1e-3, atol=1e-2)
+
+
+def test_replace_conv2d():
+    model = nn.Sequential(
+        nn.Conv2d(3, 64, 3, padding=1, bias=False), nn.ReLU(),
+        nn.Conv2d(64, 128, 3, stride=2, padding=1), nn.ReLU(),
+        nn.Conv2d(128, 128, 3, padding=1, bias=True), nn.ReLU(),
+        nn.Conv2d(128, 256, 1)).cuda()
+    assert replace_conv2d_with_nova(model, verbose=False) == 2
+    assert isinstance(model[0], NovaWinogradConv2d)
+    assert not isinstance(model[2], NovaWinogradConv2d)
+    assert isinstance(model[4], NovaWinogradConv2d)
+    out = model.half()(torch.randn(1, 3, 32, 32, device="cuda", dtype=torch.float16))
+    assert out.shape == (1, 256, 16, 16) and torch.isfinite(out).all()
+
+
+def test_training_step():
+    conv = NovaWinogradConv2dTrainable(32, 64, kernel_size=3, padding=1, bias=True).cuda()
+    opt = torch.optim.SGD(conv.parameters(), lr=0.01)
+    x = torch.randn(2, 32, 14, 14, device="cuda")
+    target = torch.randn(2, 64, 14, 14, device="cuda", dtype=torch.float16)
+    losses = []
+    for _ in range(3):
+        opt.zero_grad()
+        loss = F.mse_loss(conv(x), target)
+        loss.backward()
+        opt.step()
+        losses.append(loss.item())
+    assert losses[-1] < losses[0], losses
+    assert conv.weight.grad is not None
+
+
+def test_torch_compile():
+    conv = NovaWinogradConv2dCompilable(64, 128, kernel_size=3, padding=1).cuda()
+    x = torch.randn(2, 64, 28, 28, device="cuda", dtype=torch.float16)
+    with torch.no_grad():
+        eager = conv(x)
+        compiled = torch.compile(conv, fullgraph=True)(x)
+    assert torch.equal(eager, compiled)
+    assert torch.isfinite(compiled).all()
+
+
+def test_module_matches_oracle_bar():
+    """Stricter than the reference suite: config 1 through the module against the oracle."""
+    x, w = o.synthetic_case(1, 64, 64, 56, 56, seed=1234)
+    conv = NovaWinogradConv2d(64, 64).cuda()
+    with torch.no_grad():
+        conv.weight.copy_(torch.from_numpy(w))
+    y = conv(torch.from_numpy(x).cuda()).cpu().numpy()
+    y_ref = o.nova_forward(x, w, 1, "ref")
+    d = o.direct_conv_fp64(x, w, 1)
+    assert o.rel_l2(y, y_ref) < 2e-3
+    assert o.rel_l2(y, d) <= 1.1 * o.rel_l2(y_ref, d)
+
+
+def test_module_on_side_stream_and_cuda_graph():
+    conv = NovaWinogradConv2d(64, 64).cuda()
+    x = torch.randn(2, 64, 28, 28, device="cuda", dtype=torch.float16)
+    ref = conv(x).clone()
+    s = torch.cuda.Stream()
+    with torch.cuda.stream(s):
+        out = conv(x)
+    s.synchronize()
+    assert torch.equal(out, ref)
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        out_g = conv(x)
+    g.replay()
+    torch.cuda.synchronize()
+    assert torch.equal(out_g, ref)
+
+
+def test_handle_follows_module_device_and_dtype_conversion():
+    conv = NovaWinogradConv2d(16, 32, bias=True).cuda().half()  # weights cast to FP16 by .half()
+    x = torch.randn(1, 16, 12, 12, device="cuda", dtype=torch.float16)
+    ref = F.conv2d(x.float(), conv.weight.float(), conv.bias.float(), padding=1)
+    out = conv(x)
+    assert (torch.norm(out.float() - ref) / torch.norm(ref)).item() < 0.06
+    assert ops.get_lib().nova_get_last_error(conv._handle) == 0
