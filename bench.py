@@ -1,0 +1,507 @@
+#!/usr/bin/env python3
+"""Benchmark of the NOVA F(6,3) Winograd conv forward on B200.
+
+Workload: the ResNet-50 3x3 stride-1 layer sweep
+C = K = 64 @ 56x56, 128 @ 28x28, 256 @ 14x14, 512 @ 7x7, FP16 N(0,1) inputs,
+FP32 Kaiming-normal weights, synthetic seeded data.  One step = one forward of
+each of the four layers at batch --batch (default 128, the sweep's largest) per
+GPU.  Metric: effective TFLOP/s = direct-conv FLOPs (2*B*K*C*H_out*W_out*9) /
+time.  Multi-GPU: one process per GPU, each runs the same per-GPU batch (batch
+partitioning, no collective on the data path) -> weak scaling.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--batch B] [--impl nova|reference]
+
+Prints one JSON line on rank 0.  --impl reference times the reference's CPU
+implementation of this path (the NOVA transform math, restated in
+oracle/nova_oracle.py because the reference's HIP code cannot run here) on the
+host cores, on a bounded sample of the same workload.
+"""
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+for _p in (os.path.join(ROOT, "nova-wino-amd_b200"), os.path.join(ROOT, "oracle")):
+    if _p not in sys.path:
+        sys.path.insert(0, _p)
+
+LAYERS = [  # (name, C = K, H = W)
+    ("conv2_x", 64, 56),
+    ("conv3_x", 128, 28),
+    ("conv4_x", 256, 14),
+    ("conv5_x", 512, 7),
+]
+METRIC = "F(6,3) conv eff. TFLOP/s (direct-conv FLOPs / time), ResNet-50 3x3 s1 layer sweep"
+UNIT = "TFLOP/s"
+L2_BYTES = 126 * 1024 * 1024
+
+
+def direct_flops(B, C, K, H):
+    return 2.0 * B * K * C * H * H * 9
+
+
+def live_tiles(H):
+    return -(-H // 6)
+
+
+def load_peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            p = json.load(f)
+        return {"hbm_gbs": float(p["hbm_gbs"]), "bf16_tflops": float(p["bf16_tflops"]),
+                "bf16_tflops_sustained": float(p.get("bf16_tflops_sustained", p["bf16_tflops"])),
+                "source": "measured"}
+    except Exception:
+        return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0,
+                "source": "fallback"}
+
+
+# ---------------------------------------------------------------------------
+# CPU side: the oracle restatement of the reference's NOVA math.
+# ---------------------------------------------------------------------------
+
+def cpu_nova_sample(batch, seconds_budget=12.0):
+    """Times the NOVA FP32 math (reference precision) on the host on a bounded
+    sample: each sweep layer at `batch`, filter transform precomputed (the GPU
+    path caches it too).  Returns (TFLOP/s, threads, sample text, extra)."""
+    import numpy as np
+    import nova_oracle as o
+    cases = []
+    for name, C, H in LAYERS:
+        x, w = o.synthetic_case(batch, C, C, H, H, seed=1234 + C)
+        U = o.filter_transform(w, "ref")
+        cases.append((name, C, H, x, U))
+
+    def one_pass():
+        for name, C, H, x, U in cases:
+            nh = nw = live_tiles(H)
+            V = o.input_transform(x, nh, nw, 1, "ref")
+            M = o.gemm(U, V, "ref")
+            o.output_transform(M, batch, nh, nw, H, H, "ref")
+
+    one_pass()  # warm-up
+    reps, t0 = 0, time.perf_counter()
+    while True:
+        one_pass()
+        reps += 1
+        el = time.perf_counter() - t0
+        if el > seconds_budget or reps >= 20:
+            break
+    flops = reps * sum(direct_flops(batch, C, C, H) for _, C, H in LAYERS)
+    threads = len(os.sched_getaffinity(0))
+    sample = f"{reps} pass(es) of the 4 sweep layers at batch {batch}"
+    extra = {}
+    try:  # F.conv2d FP32 on the same sample, for context
+        import torch
+        import torch.nn.functional as F
+        torch.set_num_threads(threads)
+        xs = [torch.from_numpy(c[3].astype(np.float32)) for c in cases]
+        ws = [torch.randn(C, C, 3, 3) for _, C, _ in LAYERS]
+        for xx, ww in zip(xs, ws):
+            F.conv2d(xx, ww, padding=1)
+        t1 = time.perf_counter()
+        for xx, ww in zip(xs, ws):
+            F.conv2d(xx, ww, padding=1)
+        dt = time.perf_counter() - t1
+        extra["torch_conv2d_fp32_tflops"] = sum(direct_flops(batch, C, C, H)
+                                                for _, C, H in LAYERS) / dt / 1e12
+    except Exception as e:  # pragma: no cover
+        extra["torch_conv2d_fp32_error"] = str(e)
+    return flops / el / 1e12, threads, sample, extra
+
+
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    cpu_batch = args.cpu_batch
+    for _ in range(max(1, args.warmup)):
+        cpu_nova_sample(cpu_batch, seconds_budget=2.0)
+    vals, sample, threads = [], "", 1
+    for _ in range(args.steps):
+        v, threads, sample, _ = cpu_nova_sample(cpu_batch, seconds_budget=4.0)
+        vals.append(v)
+    value = statistics.median(vals)
+    flops_step = sum(direct_flops(cpu_batch, C, C, H) for _, C, H in LAYERS)
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT,
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": flops_step / (value * 1e12) * 1e3,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (seeded N(0,1) FP16 inputs, Kaiming-normal FP32 weights)",
+        "config": {"workload": "resnet50_3x3_sweep", "layers": [l[0] for l in LAYERS],
+                   "batch_per_step": cpu_batch, "l2": "n/a (host)"},
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port",
+                         "sample": sample},
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "note": "reference is HIP/rocBLAS for MI300X and cannot run here; its NOVA math is "
+                "timed as the numpy restatement (oracle/nova_oracle.py) on the host cores",
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ---------------------------------------------------------------------------
+# GPU side.
+# ---------------------------------------------------------------------------
+
+class ClockSampler:
+    """nvidia-smi clock / throttle sampling during the timed region."""
+
+    FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
+              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+              "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_id):
+        self.gpu_id = gpu_id
+        self.proc = None
+        self.path = None
+
+    def start(self):
+        try:
+            fd, self.path = tempfile.mkstemp(suffix=".csv")
+            os.close(fd)
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.gpu_id), f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "100"],
+                stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["sampler unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        rows = []
+        with open(self.path) as f:
+            for line in f:
+                parts = [p.strip() for p in line.split(",")]
+                if len(parts) == 7:
+                    rows.append(parts)
+        os.unlink(self.path)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"], "samples": 0}
+        sm = [float(r[0]) for r in rows if r[0].replace(".", "").isdigit()]
+        smax = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[3 + i] == "Active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": max(smax) if smax else None, "reasons": reasons,
+                "samples": len(rows)}
+
+
+def setup_dist():
+    import torch
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dist = None
+    if world > 1:
+        import torch.distributed as dist
+        dist.init_process_group("nccl", device_id=torch.device("cuda", local))
+    return world, rank, local, dist
+
+
+def barrier(dist):
+    import torch
+    if dist is not None:
+        dist.barrier()
+    torch.cuda.synchronize()
+
+
+def max_over_ranks(dist, value):
+    import torch
+    if dist is None:
+        return value
+    t = torch.tensor([value], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def build_layers(batch, device):
+    import numpy as np
+    import torch
+    from nova_winograd import NovaWinogradConv2d
+    layers = []
+    for name, C, H in LAYERS:
+        rng = np.random.default_rng(1234 + C)
+        x = torch.from_numpy(rng.standard_normal((batch, C, H, H), dtype=np.float32)).to(
+            device=device, dtype=torch.float16)
+        w = torch.from_numpy(rng.standard_normal((C, C, 3, 3), dtype=np.float32)
+                             * np.float32(np.sqrt(2.0 / (9 * C))))
+        conv = NovaWinogradConv2d(C, C, kernel_size=3, padding=1).to(device)
+        with torch.no_grad():
+            conv.weight.copy_(w)
+        layers.append((name, C, H, conv, x))
+    return layers
+
+
+def make_flush(device):
+    import torch
+    wr = torch.empty(2 * L2_BYTES // 4, dtype=torch.float32, device=device)
+    rd = torch.ones(2 * L2_BYTES // 4, dtype=torch.float32, device=device)
+
+    def flush():
+        # Write a buffer twice the L2 size, then read another one: the read
+        # evicts the dirty lines the write left, so their write-back does not
+        # land on the next timed kernel.
+        wr.fill_(1.0)
+        rd.sum()
+    return flush
+
+
+def time_kernel(fn, reps, flush):
+    """Average device time (ms) of fn() with an L2 flush between launches."""
+    import torch
+    evs = []
+    for _ in range(reps):
+        flush()
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        fn()
+        e.record()
+        evs.append((s, e))
+    torch.cuda.synchronize()
+    return sum(s.elapsed_time(e) for s, e in evs) / reps
+
+
+def stage_profile(layers, batch, flush, reps=10):
+    """Per-stage device times through the stage C-ABI entries (one launch each,
+    whole batch), with the algorithmic bytes / FLOPs of each launch."""
+    import torch
+    from nova_winograd import ops
+    lib = ops.get_lib()
+    out = []
+    for name, C, H, conv, x in layers:
+        nt = live_tiles(H)
+        BP = batch * nt * nt
+        V = torch.empty(64, BP, C, dtype=torch.float16, device=x.device)
+        M = torch.empty(64, BP, C, dtype=torch.float16, device=x.device)
+        y = torch.empty(batch, C, H, H, dtype=torch.float16, device=x.device)
+        conv(x)  # make sure the handle holds the weights
+        h = conv._handle
+        s = ops.stream_ptr()
+
+        def it():
+            ops.check(lib.nova_input_transform_v2(ops.ptr(x), ops.ptr(V), batch, C, H, H, 1,
+                                                  nt, nt, BP, s), "input_transform")
+
+        def gm():
+            ops.check(lib.nova_batched_gemm_v2(h, ops.ptr(V), ops.ptr(M), BP, s), "gemm")
+
+        def ot():
+            ops.check(lib.nova_output_transform_v2(ops.ptr(M), ops.ptr(y), batch, C, H, H,
+                                                   nt, nt, BP, s), "output_transform")
+
+        x_b = y_b = batch * C * H * H * 2
+        v_b = m_b = 64 * BP * C * 2
+        u_b = 64 * C * C * 2
+        gflop = 2.0 * 64 * C * C * BP
+        for kname, fn, nbytes, flops in (
+                ("input_transform_kernel", it, x_b + v_b, 0.0),
+                ("gemm_tc_kernel", gm, v_b + u_b + m_b, gflop),
+                ("output_transform_kernel", ot, m_b + y_b, 0.0)):
+            ms = time_kernel(fn, reps, flush)
+            out.append({"layer": name, "kernel": kname, "ms": ms, "bytes": nbytes,
+                        "flops": flops, "gbs": nbytes / ms / 1e6,
+                        "tflops": flops / ms / 1e9 if flops else None})
+    return out
+
+
+def roofline_from_stages(stages, peaks):
+    by_kernel = {}
+    for s in stages:
+        d = by_kernel.setdefault(s["kernel"], {"ms": 0.0, "bytes": 0.0, "flops": 0.0, "n": 0})
+        d["ms"] += s["ms"]
+        d["bytes"] += s["bytes"]
+        d["flops"] += s["flops"]
+        d["n"] += 1
+    top = max(by_kernel, key=lambda k: by_kernel[k]["ms"])
+    d = by_kernel[top]
+    t_hbm = d["bytes"] / (peaks["hbm_gbs"] * 1e9)
+    t_tc = d["flops"] / (peaks["bf16_tflops"] * 1e12)
+    if t_tc > t_hbm:
+        achieved = d["flops"] / (d["ms"] / 1e3) / 1e12
+        rl = {"bound": "tensor", "achieved": achieved, "peak": peaks["bf16_tflops"],
+              "unit": "TFLOP/s", "frac": achieved / peaks["bf16_tflops"]}
+    else:
+        achieved = d["bytes"] / (d["ms"] / 1e3) / 1e9
+        rl = {"bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s",
+              "frac": achieved / peaks["hbm_gbs"]}
+    tot = sum(x["ms"] for x in by_kernel.values())
+    rl.update({"kernel": top, "launches_per_step": d["n"], "avg_launch_ms": d["ms"] / d["n"],
+               "traffic": None, "peak_source": peaks["source"],
+               "shares": {k: v["ms"] / tot for k, v in by_kernel.items()}})
+    return rl
+
+
+def b1_latency(device, reps=200):
+    """Per-layer batch-1 latency (us): back-to-back module calls (host overhead
+    included) and the same call replayed from a CUDA graph (device only)."""
+    import torch
+    layers = build_layers(1, device)
+    res = {}
+    for name, C, H, conv, x in layers:
+        for _ in range(20):
+            conv(x)
+        torch.cuda.synchronize()
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        for _ in range(reps):
+            conv(x)
+        e.record()
+        torch.cuda.synchronize()
+        us_eager = s.elapsed_time(e) / reps * 1e3
+        g = torch.cuda.CUDAGraph()
+        st = torch.cuda.Stream()
+        with torch.cuda.stream(st):
+            conv(x)
+            st.synchronize()
+            with torch.cuda.graph(g, stream=st):
+                for _ in range(10):
+                    conv(x)
+        torch.cuda.synchronize()
+        g.replay()
+        torch.cuda.synchronize()
+        s.record()
+        for _ in range(reps // 10):
+            g.replay()
+        e.record()
+        torch.cuda.synchronize()
+        us_graph = s.elapsed_time(e) / reps * 1e3
+        res[name] = {"us_eager": round(us_eager, 2), "us_graph": round(us_graph, 2),
+                     "eff_tflops_graph": round(direct_flops(1, C, C, H) / us_graph / 1e6, 2)}
+    return res
+
+
+def run_nova(args):
+    import torch
+    world, rank, local, dist = setup_dist()
+    device = torch.device("cuda", local)
+    peaks = load_peaks()
+    batch = args.batch
+    layers = build_layers(batch, device)
+    flops_step = sum(direct_flops(batch, C, C, H) for _, C, H in LAYERS)
+    flush = make_flush(device)
+
+    def step():
+        for _, _, _, conv, x in layers:
+            conv(x)
+
+    for _ in range(args.warmup):
+        step()
+    barrier(dist)
+    uuid = str(torch.cuda.get_device_properties(device).uuid)
+    sampler = ClockSampler(uuid if uuid.startswith("GPU-") else f"GPU-{uuid}")
+    sampler.start()
+    time.sleep(0.3)
+    evs = []
+    for _ in range(args.steps):
+        flush()
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        step()
+        e.record()
+        evs.append((s, e))
+    torch.cuda.synchronize()
+    barrier(dist)
+    clocks = sampler.stop()
+    step_ms = [s.elapsed_time(e) for s, e in evs]
+    total_ms = max_over_ranks(dist, sum(step_ms))
+    ms_per_step = total_ms / args.steps
+    value = world * flops_step * args.steps / (total_ms / 1e3) / 1e12
+    from nova_winograd import ops
+    windows = 1
+    launches = 3 * len(LAYERS) * args.steps * windows
+
+    # End to end through the public module API: pinned host input -> device,
+    # forward, output -> pinned host, every step.
+    hx = [x.cpu().pin_memory() for _, _, _, _, x in layers]
+    hy = [torch.empty(batch, C, H, H, dtype=torch.float16).pin_memory() for _, C, H, _, _ in layers]
+    dx = [torch.empty_like(x) for _, _, _, _, x in layers]
+    h2d = sum(t.numel() * 2 for t in hx)
+    d2h = sum(t.numel() * 2 for t in hy)
+
+    def e2e_step():
+        for i, (_, _, _, conv, _) in enumerate(layers):
+            dx[i].copy_(hx[i], non_blocking=True)
+            hy[i].copy_(conv(dx[i]), non_blocking=True)
+
+    for _ in range(max(1, args.warmup)):
+        e2e_step()
+    barrier(dist)
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    for _ in range(args.steps):
+        e2e_step()
+    e.record()
+    torch.cuda.synchronize()
+    e2e_ms = max_over_ranks(dist, s.elapsed_time(e))
+    e2e_value = world * flops_step * args.steps / (e2e_ms / 1e3) / 1e12
+
+    stages = roofline = lat = cpu = None
+    if rank == 0:
+        stages = stage_profile(layers, batch, flush)
+        roofline = roofline_from_stages(stages, peaks)
+        lat = b1_latency(device)
+        if world == 1 and not args.no_cpu:
+            v, threads, sample, extra = cpu_nova_sample(args.cpu_batch)
+            cpu = {"value": v, "unit": UNIT, "cores": threads, "kind": "port", "sample": sample}
+            cpu.update(extra)
+    barrier(dist)
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_per_step,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f16",
+            "data": "synthetic (seeded N(0,1) FP16 inputs, Kaiming-normal FP32 weights)",
+            "config": {"workload": "resnet50_3x3_sweep", "layers": [l[0] for l in LAYERS],
+                       "batch_per_gpu": batch, "parallelism": f"dp{world} (batch-partitioned)",
+                       "l2": "flushed between steps (write then read 2x L2)"},
+            "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d,
+                    "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms / args.steps},
+            "gpu_launches": launches,
+            "roofline": roofline,
+            "clocks": clocks,
+            "cpu_baseline": cpu,
+            "stages": [{k: (round(v, 5) if isinstance(v, float) else v) for k, v in st.items()}
+                       for st in stages],
+            "b1_latency_us": lat,
+            "step_ms": [round(t, 4) for t in step_ms],
+            "library": ops.get_lib().nova_version().decode(),
+        }
+        print(json.dumps(line), flush=True)
+    if dist is not None:
+        dist.destroy_process_group()
+
+
+def main():
+    ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--batch", type=int, default=128)
+    ap.add_argument("--cpu-batch", type=int, default=1)
+    ap.add_argument("--impl", choices=["nova", "reference"], default="nova")
+    ap.add_argument("--no-cpu", action="store_true")
+    args = ap.parse_args()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        args.warmup = max(3, args.warmup)
+        run_nova(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -113,6 +113,13 @@ int nova_input_transform_v2(const void* d_input, void* d_V_gemm, int batch, int 
 int nova_output_transform_v2(const void* d_M_gemm, void* d_output, int batch, int K, int H_out,
                              int W_out, int nh, int nw, int BP, void* stream);
 
+/* Stage entry for the 64-way batched GEMM the reference ran through rocBLAS
+ * gemm_strided_batched_ex (csrc/nova_winograd.hip:534-548):
+ * M[pos][bp][k] = sum_c V[pos][bp][c] * U[pos][c][k], FP16 in, FP32 accumulate,
+ * FP16 out, on the handle's U, with the path nova_set_path selects. */
+int nova_batched_gemm_v2(nova_handle_t h, const void* d_V_gemm, void* d_M_gemm, int BP,
+                         void* stream);
+
 /* Bytes of caller workspace nova_forward_workspace needs (V + M), the
  * reference's sizing (csrc/nova_winograd_fused.hip:524-534 for the 3-pass case). */
 long long nova_workspace_bytes(nova_handle_t h, int batch, int H, int W, int pad);

@@ -429,6 +429,33 @@ NOVA_EXPORT int nova_forward_workspace_v2(nova_handle_t h, const void* d_input, 
                                  pad, nh, nw, as_stream(stream));
 }
 
+NOVA_EXPORT int nova_batched_gemm_v2(nova_handle_t h, const void* d_V_gemm, void* d_M_gemm,
+                                     int BP, void* stream) {
+  Context* ctx = as_ctx(h);
+  if (!ctx) return nova::fail(nullptr, NOVA_ERR_INVALID_ARGUMENT, "batched_gemm: null handle");
+  if (!ctx->has_weights) return nova::fail(ctx, NOVA_ERR_NO_WEIGHTS, "batched_gemm: no weights");
+  if (BP < 0 || (BP > 0 && (!d_V_gemm || !d_M_gemm)))
+    return nova::fail(ctx, NOVA_ERR_INVALID_ARGUMENT, "batched_gemm: bad arguments");
+  if (BP == 0) return nova::ok(ctx);
+  nova::DeviceGuard g(ctx->device);
+  const __half* V = static_cast<const __half*>(d_V_gemm);
+  __half* M = static_cast<__half*>(d_M_gemm);
+  const int path = nova::choose_path(ctx);
+  cudaError_t e;
+  if (path == 1) {
+    const char* why = "";
+    e = nova::tc_gemm_run(ctx->plan, V, M, BP, ctx->d_status, ctx->num_sms, as_stream(stream),
+                          &why);
+    if (e != cudaSuccess)
+      return nova::fail(ctx, NOVA_ERR_CUDA, std::string("batched_gemm: tcgen05 GEMM: ") + why);
+  } else {
+    e = nova::launch_gemm_simt(V, ctx->U, M, BP, ctx->C, ctx->K, as_stream(stream));
+    if (e != cudaSuccess) return nova::cuda_fail(ctx, e, "batched_gemm: SIMT GEMM");
+  }
+  ctx->last_path = path;
+  return nova::ok(ctx);
+}
+
 NOVA_EXPORT long long nova_workspace_bytes(nova_handle_t h, int batch, int H, int W, int pad) {
   Context* ctx = as_ctx(h);
   if (!ctx || !ctx->has_weights || batch < 0) return -1;

@@ -151,9 +151,35 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
 
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+      "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+        "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
 __device__ __forceinline__ uint32_t pack_half2(uint32_t a, uint32_t b) {
   __half2 h = __floats2half2_rn(__uint_as_float(a), __uint_as_float(b));
   return *reinterpret_cast<uint32_t*>(&h);
+}
+
+// FP32 accumulator bits -> FP16, written as kVec 16-byte stores (8 columns each).
+template <int kVec>
+__device__ __forceinline__ void store_row_f16(__half* dst, const uint32_t* r) {
+  uint4* o = reinterpret_cast<uint4*>(dst);
+#pragma unroll
+  for (int v = 0; v < kVec; ++v) {
+    uint4 w;
+    w.x = pack_half2(r[8 * v + 0], r[8 * v + 1]);
+    w.y = pack_half2(r[8 * v + 2], r[8 * v + 3]);
+    w.z = pack_half2(r[8 * v + 4], r[8 * v + 5]);
+    w.w = pack_half2(r[8 * v + 6], r[8 * v + 7]);
+    o[v] = w;
+  }
 }
 
 __global__ void __launch_bounds__(kThreads, 1)
@@ -288,21 +314,16 @@ __global__ void __launch_bounds__(kThreads, 1)
       const long long bp = (long long)bpt * kBM + row;
       __half* out = p.M + ((long long)pos * p.BP + bp) * p.K + (long long)kt * p.BN;
       const uint32_t taddr = tmem_base + ((uint32_t)(q * 32) << 16) + acc * (uint32_t)p.BN;
-      for (int j = 0; j < p.BN / 32; ++j) {
+      int j = 0;
+      for (; j + 32 <= p.BN; j += 32) {
         uint32_t r[32];
-        tmem_ld32(taddr + j * 32, r);
-        if (bp < p.BP) {
-          uint4* o = reinterpret_cast<uint4*>(out + j * 32);
-#pragma unroll
-          for (int v = 0; v < 4; ++v) {
-            uint4 w;
-            w.x = pack_half2(r[8 * v + 0], r[8 * v + 1]);
-            w.y = pack_half2(r[8 * v + 2], r[8 * v + 3]);
-            w.z = pack_half2(r[8 * v + 4], r[8 * v + 5]);
-            w.w = pack_half2(r[8 * v + 6], r[8 * v + 7]);
-            o[v] = w;
-          }
-        }
+        tmem_ld32(taddr + j, r);
+        if (bp < p.BP) store_row_f16<4>(out + j, r);
+      }
+      if (j < p.BN) {  // BN is a multiple of 16: at most one 16-column tail
+        uint32_t r[16];
+        tmem_ld16(taddr + j, r);
+        if (bp < p.BP) store_row_f16<2>(out + j, r);
       }
       tc_fence_before();
       mbar_arrive(smem_u32(&tempty[acc]));

@@ -54,6 +54,7 @@ SIGNATURES = {
     "nova_filter_transform_v2": (c_int, [c_void_p, c_void_p, c_int, c_int, c_void_p]),
     "nova_input_transform_v2": (c_int, [c_void_p, c_void_p] + [c_int] * 8 + [c_void_p]),
     "nova_output_transform_v2": (c_int, [c_void_p, c_void_p] + [c_int] * 7 + [c_void_p]),
+    "nova_batched_gemm_v2": (c_int, [c_void_p, c_void_p, c_void_p, c_int, c_void_p]),
     "nova_workspace_bytes": (c_longlong, [c_void_p, c_int, c_int, c_int, c_int]),
     "nova_set_path": (c_int, [c_void_p, c_int]),
     "nova_get_path": (c_int, [c_void_p]),
