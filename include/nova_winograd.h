@@ -136,6 +136,20 @@ int nova_get_path(nova_handle_t h);
  * call (and clears the flag); NOVA_OK otherwise. */
 int nova_device_status(nova_handle_t h);
 
+/* Forward that allocates nothing -- no counterpart in the reference.  For
+ * callers that may not allocate device memory where they run the convolution
+ * (a plugin inside a runtime that owns all device memory, an allocation-free
+ * real-time loop): no handle, the caller passes x, the transformed filter U in
+ * the reference layout [64][C][K] (fill it once with nova_filter_transform into
+ * memory the caller owns) and y.  V and M live in one fixed 32 MiB device array
+ * inside the library (held by every GPU that loads it): shapes whose
+ * 64*(C+K)*batch*ceil(H_out/6)*ceil(W_out/6) FP16 values exceed it are refused
+ * with NOVA_ERR_WORKSPACE.  The first call on a device looks the array's address
+ * up (make it before any stream capture); calls that overlap on the GPU share
+ * the array and race.  Returns a NOVA_* status. */
+int nova_forward_noalloc(const void* d_input, const void* d_U_gemm, void* d_output, int batch,
+                         int C, int K, int H, int W, int pad, void* stream);
+
 /* Library version string. */
 const char* nova_version(void);
 

@@ -264,6 +264,9 @@ int forward_caller_ws(Context* ctx, const void* x, void* y, void* V, void* M, in
 }
 
 }  // namespace
+
+int record_error(int code, const std::string& msg) { return fail(nullptr, code, msg); }
+
 }  // namespace nova
 
 using nova::Context;

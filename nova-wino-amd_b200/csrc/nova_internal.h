@@ -5,9 +5,15 @@
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
+#include <string>
+
 #include "nova_common.cuh"
 
 namespace nova {
+
+// Records code + message as the calling thread's last error (handle-less
+// entry points); returns code.
+int record_error(int code, const std::string& msg);
 
 // Device-side status codes written by kernels whose waits are bounded.
 enum DeviceStatus : int {

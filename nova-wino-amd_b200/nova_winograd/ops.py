@@ -59,6 +59,7 @@ SIGNATURES = {
     "nova_set_path": (c_int, [c_void_p, c_int]),
     "nova_get_path": (c_int, [c_void_p]),
     "nova_device_status": (c_int, [c_void_p]),
+    "nova_forward_noalloc": (c_int, [c_void_p, c_void_p, c_void_p] + [c_int] * 6 + [c_void_p]),
     "nova_version": (c_char_p, []),
 }
 
