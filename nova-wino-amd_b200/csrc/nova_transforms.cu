@@ -262,6 +262,8 @@ cudaError_t launch_filter_transform(const float* w, __half* U, int K, int C, boo
 
 cudaError_t launch_input_transform(const __half* x, __half* V, int B, int C, int H, int W,
                                    int pad, int nh, int nw, long long BP, cudaStream_t s) {
+  if (C % 2 == 0)
+    return launch_input_transform_fast(x, V, C, H, W, pad, nh, nw, 0, (long long)B * nh, BP, s);
   const int n_twc = (nw + kTW - 1) / kTW;
   const int n_cg = (C + kCG - 1) / kCG;
   dim3 grid(n_twc * n_cg, nh, B);
@@ -271,6 +273,9 @@ cudaError_t launch_input_transform(const __half* x, __half* V, int B, int C, int
 
 cudaError_t launch_output_transform(const __half* M, __half* y, int B, int K, int H_out,
                                     int W_out, int nh, int nw, long long BP, cudaStream_t s) {
+  if (K % 2 == 0)
+    return launch_output_transform_fast(M, y, K, H_out, W_out, nh, nw, 0, (long long)B * nh, BP,
+                                        s);
   const int n_twc = (nw + kTW - 1) / kTW;
   const int n_kg = (K + kCG - 1) / kCG;
   dim3 grid(n_twc * n_kg, nh, B);

@@ -1,0 +1,313 @@
+// Input / output transform kernels for even channel counts (the hot path).
+//
+// Geometry: a block owns one tile row (row = b*nh + th), a chunk of TPC
+// consecutive tiles along w (TPC is a template parameter, so every shared-memory
+// offset below is a compile-time immediate) and 64*G channels.  Work item =
+// (tile, 64 channels) for one warp; each lane owns two adjacent channels, so
+// every access a warp makes to one position of V or M is one aligned half2 per
+// lane = one full 128-byte line.
+//
+// Input transform:  image rows staged in shared memory [row][col][channel]
+//   (66-half cell pitch = 33 words, odd: conflict-free both for the row-wise
+//   staging stores and for the lane-pair reads), then V = B^T d B in
+//   registers, written straight to V[pos][bp][c].
+// Output transform: M read straight from M[pos][bp][k] (64 independent loads per
+//   lane), Y = A M A^T in registers, parked in shared memory [row][col][k], then
+//   written as whole output row segments along w (warp per row, lane per
+//   column).
+// Reference: input_transform_kernel(_mt) and output_transform_kernel(_mt),
+// Jayluci4/nova-wino-amd csrc/nova_winograd.hip:141-205, 264-328, 338-450.
+#include <algorithm>
+
+#include "nova_internal.h"
+
+namespace nova {
+namespace fast {
+
+constexpr int kMaxTPC = 6;
+constexpr long long kMaxGridY = 65535;
+
+struct Args {
+  int C, H, W, pad;  // C = channels of this tensor (C for input, K for output)
+  int nh, nw;
+  long long row0;    // first global tile row of the window
+  long long lrow0;   // window-relative tile row of blockIdx.y == 0
+  long long BP;      // bp extent (plane stride) of V / M
+  int n_twc;         // chunks along w
+};
+
+template <int TPC, int G>
+struct Geo {
+  static constexpr int kCGN = 64 * G;            // channels per block
+  static constexpr int kPitch = kCGN + 2;        // halves per staged cell (odd words)
+  static constexpr int kInCols = TPC * 6 + 2;    // staged image columns
+  static constexpr int kOutCols = TPC * 6;       // output columns per chunk
+  static constexpr int kWarps = TPC * G < 2 ? 2 : TPC * G;
+  static constexpr size_t kInSmem = 8 * kInCols * kPitch * 2;
+  static constexpr size_t kOutSmem = 6 * kOutCols * kPitch * 2;
+};
+
+__device__ __forceinline__ void block_coords(const Args& a, long long& lrow, int& b, int& th,
+                                             int& twc, int& cg) {
+  twc = blockIdx.x % a.n_twc;
+  cg = blockIdx.x / a.n_twc;
+  lrow = a.lrow0 + blockIdx.y;
+  const long long grow = a.row0 + lrow;
+  b = (int)(grow / a.nh);
+  th = (int)(grow - (long long)b * a.nh);
+}
+
+template <int TPC, int G>
+__global__ void __launch_bounds__(32 * Geo<TPC, G>::kWarps)
+    input_transform_fast(const __half* __restrict__ x, __half* __restrict__ V, const Args a) {
+  using Gm = Geo<TPC, G>;
+  __shared__ __align__(16) __half xs[8 * Gm::kInCols * Gm::kPitch];
+  long long lrow;
+  int b, th, twc, cg;
+  block_coords(a, lrow, b, th, twc, cg);
+  const int C = a.C, H = a.H, W = a.W;
+  const int c0 = cg * Gm::kCGN;
+  const int tw0 = twc * TPC;
+  const int ntw = min(TPC, a.nw - tw0);
+  const int h0 = th * 6 - a.pad;
+  const int w0 = tw0 * 6 - a.pad;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+  // Stage rows h0..h0+7 of the block's channels, columns w0..w0+kInCols-1.
+  // A warp takes whole channels (kChanInFlight at a time: 16 loads per channel
+  // per lane in flight); the 8 rows of a channel are one base pointer plus
+  // per-block row offsets, and every shared-memory offset is an immediate.
+  {
+    const bool ok0 = lane < Gm::kInCols && w0 + lane >= 0 && w0 + lane < W;
+    const bool ok1 = lane + 32 < Gm::kInCols && w0 + lane + 32 >= 0 && w0 + lane + 32 < W;
+    unsigned rmask = 0;  // bit r: image row h0 + r exists
+    int roff[8];
+#pragma unroll
+    for (int r = 0; r < 8; ++r) {
+      const int h = h0 + r;
+      if (h >= 0 && h < H) rmask |= 1u << r;
+      roff[r] = (h >= 0 && h < H ? h : 0) * W;
+    }
+    const long long plane_x = (long long)H * W;
+    const __half* xb = x + ((long long)b * C + c0) * plane_x + w0;
+    __half* sbase = xs + lane * Gm::kPitch;
+    constexpr int kChanInFlight = 2;
+    for (int cl0 = warp; cl0 < Gm::kCGN; cl0 += Gm::kWarps * kChanInFlight) {
+      __half2 v[kChanInFlight][8];
+#pragma unroll
+      for (int u = 0; u < kChanInFlight; ++u) {
+        const int cl = cl0 + u * Gm::kWarps;
+        const bool cok = cl < Gm::kCGN && c0 + cl < C;
+        const __half* cp = xb + (cok ? cl : 0) * plane_x;
+#pragma unroll
+        for (int r = 0; r < 8; ++r) {
+          const bool rok = cok && ((rmask >> r) & 1u);
+          v[u][r].x = (rok && ok0) ? cp[roff[r] + lane] : __ushort_as_half(0);
+          v[u][r].y = (rok && ok1) ? cp[roff[r] + lane + 32] : __ushort_as_half(0);
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < kChanInFlight; ++u) {
+        const int cl = cl0 + u * Gm::kWarps;
+        if (cl < Gm::kCGN) {
+#pragma unroll
+          for (int r = 0; r < 8; ++r) {
+            if (lane < Gm::kInCols) sbase[r * Gm::kInCols * Gm::kPitch + cl] = v[u][r].x;
+            if (lane + 32 < Gm::kInCols)
+              sbase[(r * Gm::kInCols + 32) * Gm::kPitch + cl] = v[u][r].y;
+          }
+        }
+      }
+    }
+  }
+  __syncthreads();
+
+  const long long plane = a.BP * (long long)C;
+  for (int it = warp; it < TPC * G; it += Gm::kWarps) {
+    const int t = it / G, g = it % G;
+    if (t >= ntw) break;
+    const int cl = g * 64 + 2 * lane;
+    const int c = c0 + cl;
+    float ta[8][8], tb[8][8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {  // columns: tmp[.][j] = B^T d[.][j]
+      float va[8], vb[8], fa[8], fb[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const __half2 p = *reinterpret_cast<const __half2*>(
+            xs + (i * Gm::kInCols + t * 6 + j) * Gm::kPitch + cl);
+        const float2 f = __half22float2(p);
+        va[i] = f.x;
+        vb[i] = f.y;
+      }
+      bt_1d(va, fa);
+      bt_1d(vb, fb);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        ta[i][j] = fa[i];
+        tb[i][j] = fb[i];
+      }
+    }
+    if (c < C) {  // C is even: the pair is wholly in or out
+      __half2* out = reinterpret_cast<__half2*>(V + (lrow * a.nw + tw0 + t) * C + c);
+#pragma unroll
+      for (int r = 0; r < 8; ++r) {  // rows: V[r][.] = tmp[r][.] B
+        float fa[8], fb[8];
+        bt_1d(ta[r], fa);
+        bt_1d(tb[r], fb);
+#pragma unroll
+        for (int s = 0; s < 8; ++s)
+          out[(long long)(r * 8 + s) * (plane >> 1)] = __floats2half2_rn(fa[s], fb[s]);
+      }
+    }
+  }
+}
+
+template <int TPC, int G>
+__global__ void __launch_bounds__(32 * Geo<TPC, G>::kWarps)
+    output_transform_fast(const __half* __restrict__ M, __half* __restrict__ y, const Args a) {
+  using Gm = Geo<TPC, G>;
+  __shared__ __align__(16) __half ys[6 * Gm::kOutCols * Gm::kPitch];
+  long long lrow;
+  int b, th, twc, kg;
+  block_coords(a, lrow, b, th, twc, kg);
+  const int K = a.C, H_out = a.H, W_out = a.W;
+  const int k0 = kg * Gm::kCGN;
+  const int tw0 = twc * TPC;
+  const int ntw = min(TPC, a.nw - tw0);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const long long plane = a.BP * (long long)K;
+
+  for (int it = warp; it < TPC * G; it += Gm::kWarps) {
+    const int t = it / G, g = it % G;
+    if (t >= ntw) break;
+    const int kl = g * 64 + 2 * lane;
+    const int k = k0 + kl;
+    const bool kok = k < K;
+    const __half2* in =
+        reinterpret_cast<const __half2*>(M + (lrow * a.nw + tw0 + t) * K + (kok ? k : 0));
+    float ta[6][8], tb[6][8];
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {  // columns: tmp[.][q] = A m[.][q]
+      float ma[8], mb[8], ga[6], gb[6];
+#pragma unroll
+      for (int p = 0; p < 8; ++p) {
+        const float2 f = kok ? __half22float2(in[(long long)(p * 8 + q) * (plane >> 1)])
+                             : make_float2(0.f, 0.f);
+        ma[p] = f.x;
+        mb[p] = f.y;
+      }
+      a_1d(ma, ga);
+      a_1d(mb, gb);
+#pragma unroll
+      for (int i = 0; i < 6; ++i) {
+        ta[i][q] = ga[i];
+        tb[i][q] = gb[i];
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < 6; ++i) {  // rows: Y[i][.] = tmp[i][.] A^T
+      float ga[6], gb[6];
+      a_1d(ta[i], ga);
+      a_1d(tb[i], gb);
+#pragma unroll
+      for (int j = 0; j < 6; ++j)
+        *reinterpret_cast<__half2*>(ys + (i * Gm::kOutCols + t * 6 + j) * Gm::kPitch + kl) =
+            __floats2half2_rn(ga[j], gb[j]);
+    }
+  }
+  __syncthreads();
+
+  // Write output rows: warp per channel (6 rows each), lane per column.
+  const int wcols = min(ntw * 6, W_out - tw0 * 6);
+  const int hrows = min(6, H_out - th * 6);
+  const long long plane_y = (long long)H_out * W_out;
+  __half* yb = y + ((long long)b * K + k0) * plane_y + (long long)(th * 6) * W_out + tw0 * 6;
+  const __half* sbase = ys + lane * Gm::kPitch;
+  const bool c0ok = lane < wcols, c1ok = lane + 32 < wcols;
+  for (int kl = warp; kl < Gm::kCGN; kl += Gm::kWarps) {
+    if (k0 + kl >= K) break;
+    __half* dst = yb + kl * plane_y;
+#pragma unroll
+    for (int r = 0; r < 6; ++r) {
+      if (r < hrows) {
+        if (c0ok) dst[r * W_out + lane] = sbase[r * Gm::kOutCols * Gm::kPitch + kl];
+        if (c1ok) dst[r * W_out + lane + 32] = sbase[(r * Gm::kOutCols + 32) * Gm::kPitch + kl];
+      }
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Host dispatch.
+// ---------------------------------------------------------------------------
+struct Plan {
+  int n_twc, tpc, G, n_cg;
+};
+
+static Plan make_plan(int nw, int C) {
+  Plan p;
+  p.n_twc = (nw + kMaxTPC - 1) / kMaxTPC;
+  p.tpc = (nw + p.n_twc - 1) / p.n_twc;
+  p.G = (p.tpc <= 2 && C >= 128) ? 2 : 1;
+  p.n_cg = (C + 64 * p.G - 1) / (64 * p.G);
+  return p;
+}
+
+template <int TPC, int G>
+static void launch_it(const __half* x, __half* V, Args a, long long nrows, unsigned gx,
+                      cudaStream_t s) {
+  for (long long done = 0; done < nrows; done += kMaxGridY) {
+    a.lrow0 = done;
+    dim3 grid(gx, (unsigned)std::min(kMaxGridY, nrows - done));
+    input_transform_fast<TPC, G><<<grid, 32 * Geo<TPC, G>::kWarps, 0, s>>>(x, V, a);
+  }
+}
+
+template <int TPC, int G>
+static void launch_ot(const __half* M, __half* y, Args a, long long nrows, unsigned gx,
+                      cudaStream_t s) {
+  for (long long done = 0; done < nrows; done += kMaxGridY) {
+    a.lrow0 = done;
+    dim3 grid(gx, (unsigned)std::min(kMaxGridY, nrows - done));
+    output_transform_fast<TPC, G><<<grid, 32 * Geo<TPC, G>::kWarps, 0, s>>>(M, y, a);
+  }
+}
+
+#define NOVA_TPC_SWITCH(TPC_VAL, G_VAL, FN, ...)                       \
+  switch ((TPC_VAL) * 4 + (G_VAL)) {                                   \
+    case 1 * 4 + 1: FN<1, 1>(__VA_ARGS__); break;                      \
+    case 1 * 4 + 2: FN<1, 2>(__VA_ARGS__); break;                      \
+    case 2 * 4 + 1: FN<2, 1>(__VA_ARGS__); break;                      \
+    case 2 * 4 + 2: FN<2, 2>(__VA_ARGS__); break;                      \
+    case 3 * 4 + 1: FN<3, 1>(__VA_ARGS__); break;                      \
+    case 4 * 4 + 1: FN<4, 1>(__VA_ARGS__); break;                      \
+    case 5 * 4 + 1: FN<5, 1>(__VA_ARGS__); break;                      \
+    default: FN<6, 1>(__VA_ARGS__); break;                             \
+  }
+
+}  // namespace fast
+
+cudaError_t launch_input_transform_fast(const __half* x, __half* V, int C, int H, int W, int pad,
+                                        int nh, int nw, long long row0, long long nrows,
+                                        long long BP, cudaStream_t s) {
+  if (nrows <= 0) return cudaSuccess;
+  const fast::Plan p = fast::make_plan(nw, C);
+  fast::Args a{C, H, W, pad, nh, nw, row0, 0, BP, p.n_twc};
+  const unsigned gx = (unsigned)(p.n_twc * p.n_cg);
+  NOVA_TPC_SWITCH(p.tpc, p.G, fast::launch_it, x, V, a, nrows, gx, s);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_output_transform_fast(const __half* M, __half* y, int K, int H_out, int W_out,
+                                         int nh, int nw, long long row0, long long nrows,
+                                         long long BP, cudaStream_t s) {
+  if (nrows <= 0) return cudaSuccess;
+  const fast::Plan p = fast::make_plan(nw, K);
+  fast::Args a{K, H_out, W_out, 0, nh, nw, row0, 0, BP, p.n_twc};
+  const unsigned gx = (unsigned)(p.n_twc * p.n_cg);
+  NOVA_TPC_SWITCH(p.tpc, p.G, fast::launch_ot, M, y, a, nrows, gx, s);
+  return cudaGetLastError();
+}
+
+}  // namespace nova
