@@ -12,7 +12,9 @@
 //   * tiles that lie wholly in the padding (the reference's over-tiling, see
 //     compute_tiling) are skipped; nova_compute_tiling still returns the
 //     reference's values and workspaces are still sized by them.
+#include <algorithm>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <string>
 
@@ -192,30 +194,71 @@ int choose_path(Context* ctx) {
 
 // The three passes.  V and M hold at least 64*C*BP and 64*K*BP halves with
 // BP = B * ceil(H_out/6) * ceil(W_out/6).
+// L2 budget for one window's V + M (bytes), from NOVA_L2_WINDOW_MB; unset or 0
+// = a single window over the whole batch.  Off by default: measured on B200 at
+// batch 128, windows of 24-80 MB were 0-40 % slower than one window because the
+// transforms are not HBM-bound and every window adds kernel drain / fill.
+size_t l2_window_bytes() {
+  static const size_t bytes = [] {
+    const char* env = std::getenv("NOVA_L2_WINDOW_MB");
+    long mb = env ? std::atol(env) : 0;
+    if (mb < 0) mb = 0;
+    return (size_t)mb << 20;
+  }();
+  return bytes;
+}
+
+// Tile rows (row = b*nh + th) per window so that the window's V and M fit the
+// L2 budget.
+long long window_rows(const Context* ctx, int nw, long long total_rows) {
+  const size_t budget = l2_window_bytes();
+  if (budget == 0) return total_rows;
+  const size_t per_row = 64ull * (size_t)(ctx->C + ctx->K) * 2 * (size_t)nw;
+  long long r = (long long)(budget / per_row);
+  if (r < 1) r = 1;
+  return std::min(r, total_rows);
+}
+
+// The three passes.  V and M hold at least 64*C*BP and 64*K*BP halves with
+// BP = B * ceil(H_out/6) * ceil(W_out/6).  For even channel counts the batch
+// is cut into windows of whole tile rows whose V and M fit in L2; each window
+// runs its three passes back to back on the front of the workspace, so V and M
+// are written and re-read in L2 instead of HBM.
 int run_forward(Context* ctx, const void* x, void* y, void* V, void* M, int B, int H, int W,
                 int pad, cudaStream_t s) {
   if (B == 0) return ok(ctx);
   int nh, nw, H_out, W_out;
   live_tiling(H, W, pad, &nh, &nw, &H_out, &W_out);
-  const long long BP = (long long)B * nh * nw;
   const __half* xh = static_cast<const __half*>(x);
   __half* Vh = static_cast<__half*>(V);
   __half* Mh = static_cast<__half*>(M);
-  cudaError_t e = launch_input_transform(xh, Vh, B, ctx->C, H, W, pad, nh, nw, BP, s);
-  if (e != cudaSuccess) return cuda_fail(ctx, e, "forward: input transform");
+  __half* yh = static_cast<__half*>(y);
   const int path = choose_path(ctx);
-  if (path == 1) {
-    const char* why = "";
-    e = tc_gemm_run(ctx->plan, Vh, Mh, BP, ctx->d_status, ctx->num_sms, s, &why);
-    if (e != cudaSuccess)
-      return fail(ctx, NOVA_ERR_CUDA, std::string("forward: tcgen05 GEMM: ") + why);
-  } else {
-    e = launch_gemm_simt(Vh, ctx->U, Mh, BP, ctx->C, ctx->K, s);
-    if (e != cudaSuccess) return cuda_fail(ctx, e, "forward: SIMT GEMM");
+  const bool even = ctx->C % 2 == 0 && ctx->K % 2 == 0;
+  const long long total_rows = (long long)B * nh;
+  const long long per_window = even ? window_rows(ctx, nw, total_rows) : total_rows;
+  for (long long r0 = 0; r0 < total_rows; r0 += per_window) {
+    const long long nrows = std::min(per_window, total_rows - r0);
+    const long long BPw = nrows * nw;
+    cudaError_t e =
+        even ? launch_input_transform_fast(xh, Vh, ctx->C, H, W, pad, nh, nw, r0, nrows, BPw, s)
+             : launch_input_transform(xh, Vh, B, ctx->C, H, W, pad, nh, nw, BPw, s);
+    if (e != cudaSuccess) return cuda_fail(ctx, e, "forward: input transform");
+    if (path == 1) {
+      const char* why = "";
+      e = tc_gemm_run(ctx->plan, Vh, Mh, BPw, ctx->d_status, ctx->num_sms, s, &why);
+      if (e != cudaSuccess)
+        return fail(ctx, NOVA_ERR_CUDA, std::string("forward: tcgen05 GEMM: ") + why);
+    } else {
+      e = launch_gemm_simt(Vh, ctx->U, Mh, BPw, ctx->C, ctx->K, s);
+      if (e != cudaSuccess) return cuda_fail(ctx, e, "forward: SIMT GEMM");
+    }
+    e = even ? launch_output_transform_fast(Mh, yh, ctx->K, H_out, W_out, nh, nw, r0, nrows, BPw,
+                                            s)
+             : launch_output_transform(Mh, yh, B, ctx->K, H_out, W_out, nh, nw, BPw, s);
+    if (e != cudaSuccess) return cuda_fail(ctx, e, "forward: output transform");
   }
   ctx->last_path = path;
-  e = launch_output_transform(Mh, static_cast<__half*>(y), B, ctx->K, H_out, W_out, nh, nw, BP, s);
-  if (e != cudaSuccess) return cuda_fail(ctx, e, "forward: output transform");
   return ok(ctx);
 }
 

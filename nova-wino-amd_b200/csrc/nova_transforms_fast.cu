@@ -25,6 +25,15 @@ namespace nova {
 namespace fast {
 
 constexpr int kMaxTPC = 6;
+#ifndef NOVA_IT_CHAN_IN_FLIGHT
+#define NOVA_IT_CHAN_IN_FLIGHT 2
+#endif
+#ifndef NOVA_IT_MIN_BLOCKS
+#define NOVA_IT_MIN_BLOCKS 3  // 128 registers: 3 blocks of 5 warps per SM
+#endif
+#ifndef NOVA_OT_MIN_BLOCKS
+#define NOVA_OT_MIN_BLOCKS 3
+#endif
 constexpr long long kMaxGridY = 65535;
 
 struct Args {
@@ -58,7 +67,7 @@ __device__ __forceinline__ void block_coords(const Args& a, long long& lrow, int
 }
 
 template <int TPC, int G>
-__global__ void __launch_bounds__(32 * Geo<TPC, G>::kWarps)
+__global__ void __launch_bounds__(32 * Geo<TPC, G>::kWarps, NOVA_IT_MIN_BLOCKS)
     input_transform_fast(const __half* __restrict__ x, __half* __restrict__ V, const Args a) {
   using Gm = Geo<TPC, G>;
   __shared__ __align__(16) __half xs[8 * Gm::kInCols * Gm::kPitch];
@@ -91,7 +100,7 @@ __global__ void __launch_bounds__(32 * Geo<TPC, G>::kWarps)
     const long long plane_x = (long long)H * W;
     const __half* xb = x + ((long long)b * C + c0) * plane_x + w0;
     __half* sbase = xs + lane * Gm::kPitch;
-    constexpr int kChanInFlight = 2;
+    constexpr int kChanInFlight = NOVA_IT_CHAN_IN_FLIGHT;
     for (int cl0 = warp; cl0 < Gm::kCGN; cl0 += Gm::kWarps * kChanInFlight) {
       __half2 v[kChanInFlight][8];
 #pragma unroll
@@ -164,7 +173,7 @@ __global__ void __launch_bounds__(32 * Geo<TPC, G>::kWarps)
 }
 
 template <int TPC, int G>
-__global__ void __launch_bounds__(32 * Geo<TPC, G>::kWarps)
+__global__ void __launch_bounds__(32 * Geo<TPC, G>::kWarps, NOVA_OT_MIN_BLOCKS)
     output_transform_fast(const __half* __restrict__ M, __half* __restrict__ y, const Args a) {
   using Gm = Geo<TPC, G>;
   __shared__ __align__(16) __half ys[6 * Gm::kOutCols * Gm::kPitch];
