@@ -248,6 +248,239 @@ __global__ void __launch_bounds__(32 * Geo<TPC, G>::kWarps, NOVA_OT_MIN_BLOCKS)
 }
 
 // ---------------------------------------------------------------------------
+// Plane mode: images of at most 3x3 tiles (e.g. 14x14, 7x7).  A block owns a
+// whole image for 64 channels.  Row-wise staging would leave most lanes idle on
+// 7- or 14-wide rows, so lanes walk the contiguous image plane instead (each
+// lane's plane elements and their shared-memory cells are computed once per
+// block), and the output is written back as whole contiguous planes.
+// ---------------------------------------------------------------------------
+template <int TR, int TC>
+struct PlaneGeo {
+  static constexpr int kRows = TR * 6 + 2, kCols = TC * 6 + 2;    // padded input
+  static constexpr int kCells = kRows * kCols;
+  static constexpr int kInPerLane = (kCells + 31) / 32;
+  static constexpr int kOutCells = 36 * TR * TC;
+  static constexpr int kOutPerLane = (kOutCells + 31) / 32;
+  static constexpr int kPitch = 66;                                // 64 channels + 2
+  static constexpr int kWarps = TR * TC < 2 ? 2 : TR * TC;
+  // Blocks per SM the register budget is sized for (about 128 registers/thread).
+  static constexpr int kMinBlocks = 65536 / (128 * 32 * kWarps) < 1 ? 1 : 65536 / (128 * 32 * kWarps);
+  static constexpr size_t kInSmem = (size_t)kCells * kPitch * 2;
+  static constexpr size_t kOutSmem = (size_t)kOutCells * kPitch * 2;
+};
+
+// Plane args: BP/row window semantics as Args; row0 and lrow0 are tile rows and
+// are multiples of nh here (blocks own whole images).
+template <int TR, int TC>
+__global__ void __launch_bounds__(32 * PlaneGeo<TR, TC>::kWarps, PlaneGeo<TR, TC>::kMinBlocks)
+    input_transform_plane(const __half* __restrict__ x, __half* __restrict__ V, const Args a) {
+  using Pg = PlaneGeo<TR, TC>;
+  extern __shared__ __align__(16) __half xs[];  // [kCells][kPitch]
+  const int cg = blockIdx.x;
+  const long long limg = a.lrow0 / TR + blockIdx.y;  // image inside the window
+  const long long b = a.row0 / TR + limg;
+  const int C = a.C, H = a.H, W = a.W, pad = a.pad;
+  const int c0 = cg * 64;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+  // Lane's padded-plane cells: global offset inside the image plane (or -1 for
+  // zero padding) and shared-memory cell offset.
+  int goff[Pg::kInPerLane], soff[Pg::kInPerLane];
+#pragma unroll
+  for (int m = 0; m < Pg::kInPerLane; ++m) {
+    const int e = lane + 32 * m;
+    const int r = e / Pg::kCols, col = e - (e / Pg::kCols) * Pg::kCols;
+    const int h = r - pad, w = col - pad;
+    soff[m] = e < Pg::kCells ? e * Pg::kPitch : -1;
+    goff[m] = (e < Pg::kCells && h >= 0 && h < H && w >= 0 && w < W) ? h * W + w : -1;
+  }
+  const long long plane_x = (long long)H * W;
+  const __half* xb = x + (b * C + c0) * plane_x;
+  for (int cl = warp; cl < 64; cl += Pg::kWarps) {
+    const bool cok = c0 + cl < C;
+    const __half* cp = xb + (cok ? cl : 0) * plane_x;
+    __half v[Pg::kInPerLane];
+#pragma unroll
+    for (int m = 0; m < Pg::kInPerLane; ++m)
+      v[m] = (cok && goff[m] >= 0) ? cp[goff[m]] : __ushort_as_half(0);
+#pragma unroll
+    for (int m = 0; m < Pg::kInPerLane; ++m)
+      if (soff[m] >= 0) xs[soff[m] + cl] = v[m];
+  }
+  __syncthreads();
+
+  const long long plane = a.BP * (long long)C;
+  for (int t = warp; t < TR * TC; t += Pg::kWarps) {
+    const int tr = t / TC, tc = t - (t / TC) * TC;
+    const int cl = 2 * lane;
+    const int c = c0 + cl;
+    float ta[8][8], tb[8][8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      float va[8], vb[8], fa[8], fb[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const float2 f = __half22float2(*reinterpret_cast<const __half2*>(
+            xs + ((tr * 6 + i) * Pg::kCols + tc * 6 + j) * Pg::kPitch + cl));
+        va[i] = f.x;
+        vb[i] = f.y;
+      }
+      bt_1d(va, fa);
+      bt_1d(vb, fb);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        ta[i][j] = fa[i];
+        tb[i][j] = fb[i];
+      }
+    }
+    if (c < C) {
+      const long long bp = (limg * TR + tr) * TC + tc;
+      __half2* out = reinterpret_cast<__half2*>(V + bp * C + c);
+#pragma unroll
+      for (int r = 0; r < 8; ++r) {
+        float fa[8], fb[8];
+        bt_1d(ta[r], fa);
+        bt_1d(tb[r], fb);
+#pragma unroll
+        for (int s = 0; s < 8; ++s)
+          out[(long long)(r * 8 + s) * (plane >> 1)] = __floats2half2_rn(fa[s], fb[s]);
+      }
+    }
+  }
+}
+
+template <int TR, int TC>
+__global__ void __launch_bounds__(32 * PlaneGeo<TR, TC>::kWarps, PlaneGeo<TR, TC>::kMinBlocks)
+    output_transform_plane(const __half* __restrict__ M, __half* __restrict__ y, const Args a) {
+  using Pg = PlaneGeo<TR, TC>;
+  extern __shared__ __align__(16) __half ys[];  // [kOutCells][kPitch]
+  const int kg = blockIdx.x;
+  const long long limg = a.lrow0 / TR + blockIdx.y;
+  const long long b = a.row0 / TR + limg;
+  const int K = a.C, H_out = a.H, W_out = a.W;
+  const int k0 = kg * 64;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const long long plane = a.BP * (long long)K;
+
+  for (int t = warp; t < TR * TC; t += Pg::kWarps) {
+    const int tr = t / TC, tc = t - (t / TC) * TC;
+    const int kl = 2 * lane;
+    const int k = k0 + kl;
+    const bool kok = k < K;
+    const long long bp = (limg * TR + tr) * TC + tc;
+    const __half2* in = reinterpret_cast<const __half2*>(M + bp * K + (kok ? k : 0));
+    float ta[6][8], tb[6][8];
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+      float ma[8], mb[8], ga[6], gb[6];
+#pragma unroll
+      for (int p = 0; p < 8; ++p) {
+        const float2 f = kok ? __half22float2(in[(long long)(p * 8 + q) * (plane >> 1)])
+                             : make_float2(0.f, 0.f);
+        ma[p] = f.x;
+        mb[p] = f.y;
+      }
+      a_1d(ma, ga);
+      a_1d(mb, gb);
+#pragma unroll
+      for (int i = 0; i < 6; ++i) {
+        ta[i][q] = ga[i];
+        tb[i][q] = gb[i];
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < 6; ++i) {
+      float ga[6], gb[6];
+      a_1d(ta[i], ga);
+      a_1d(tb[i], gb);
+#pragma unroll
+      for (int j = 0; j < 6; ++j)
+        *reinterpret_cast<__half2*>(ys + ((tr * 6 + i) * (TC * 6) + tc * 6 + j) * Pg::kPitch +
+                                    kl) = __floats2half2_rn(ga[j], gb[j]);
+    }
+  }
+  __syncthreads();
+
+  // Whole output planes: lane over the plane's elements.
+  const int HW = H_out * W_out;
+  int soff[Pg::kOutPerLane];
+#pragma unroll
+  for (int m = 0; m < Pg::kOutPerLane; ++m) {
+    const int e = lane + 32 * m;
+    const int r = e / W_out, col = e - (e / W_out) * W_out;
+    soff[m] = e < HW ? (r * (TC * 6) + col) * Pg::kPitch : -1;
+  }
+  __half* yb = y + (b * K + k0) * (long long)HW;
+  for (int kl = warp; kl < 64; kl += Pg::kWarps) {
+    if (k0 + kl >= K) break;
+    __half* dst = yb + (long long)kl * HW;
+#pragma unroll
+    for (int m = 0; m < Pg::kOutPerLane; ++m)
+      if (soff[m] >= 0) dst[lane + 32 * m] = ys[soff[m] + kl];
+  }
+}
+
+// Shared memory above 48 KB is a per-device, per-kernel opt-in.
+template <const void* (*Fn)()>
+static bool smem_optin_once(size_t bytes) {
+  static bool done[64] = {};
+  if (bytes <= 48 * 1024) return true;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return false;
+  if (done[dev]) return true;
+  done[dev] = cudaFuncSetAttribute(Fn(), cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                   (int)bytes) == cudaSuccess;
+  return done[dev];
+}
+
+template <int TR, int TC>
+const void* it_plane_fn() { return (const void*)input_transform_plane<TR, TC>; }
+template <int TR, int TC>
+const void* ot_plane_fn() { return (const void*)output_transform_plane<TR, TC>; }
+
+template <int TR, int TC>
+static void launch_it_plane(const __half* x, __half* V, Args a, long long nimg, unsigned gx,
+                            cudaStream_t s) {
+  using Pg = PlaneGeo<TR, TC>;
+  if (!smem_optin_once<it_plane_fn<TR, TC>>(Pg::kInSmem)) return;
+  for (long long done = 0; done < nimg; done += kMaxGridY) {
+    a.lrow0 = done * TR;
+    dim3 grid(gx, (unsigned)std::min(kMaxGridY, nimg - done));
+    input_transform_plane<TR, TC><<<grid, 32 * Pg::kWarps, Pg::kInSmem, s>>>(x, V, a);
+  }
+}
+
+template <int TR, int TC>
+static void launch_ot_plane(const __half* M, __half* y, Args a, long long nimg, unsigned gx,
+                            cudaStream_t s) {
+  using Pg = PlaneGeo<TR, TC>;
+  if (!smem_optin_once<ot_plane_fn<TR, TC>>(Pg::kOutSmem)) return;
+  for (long long done = 0; done < nimg; done += kMaxGridY) {
+    a.lrow0 = done * TR;
+    dim3 grid(gx, (unsigned)std::min(kMaxGridY, nimg - done));
+    output_transform_plane<TR, TC><<<grid, 32 * Pg::kWarps, Pg::kOutSmem, s>>>(M, y, a);
+  }
+}
+
+#define NOVA_PLANE_SWITCH(TR_VAL, TC_VAL, FN, ...)  \
+  switch ((TR_VAL) * 4 + (TC_VAL)) {                \
+    case 1 * 4 + 1: FN<1, 1>(__VA_ARGS__); break;   \
+    case 1 * 4 + 2: FN<1, 2>(__VA_ARGS__); break;   \
+    case 1 * 4 + 3: FN<1, 3>(__VA_ARGS__); break;   \
+    case 2 * 4 + 1: FN<2, 1>(__VA_ARGS__); break;   \
+    case 2 * 4 + 2: FN<2, 2>(__VA_ARGS__); break;   \
+    case 2 * 4 + 3: FN<2, 3>(__VA_ARGS__); break;   \
+    case 3 * 4 + 1: FN<3, 1>(__VA_ARGS__); break;   \
+    case 3 * 4 + 2: FN<3, 2>(__VA_ARGS__); break;   \
+    default: FN<3, 3>(__VA_ARGS__); break;          \
+  }
+
+// Plane mode applies to whole images of at most 3x3 tiles.
+static bool use_plane(int nh, int nw, long long row0, long long nrows) {
+  return nh <= 3 && nw <= 3 && row0 % nh == 0 && nrows % nh == 0;
+}
+
+// ---------------------------------------------------------------------------
 // Host dispatch.
 // ---------------------------------------------------------------------------
 struct Plan {
@@ -301,6 +534,12 @@ cudaError_t launch_input_transform_fast(const __half* x, __half* V, int C, int H
                                         int nh, int nw, long long row0, long long nrows,
                                         long long BP, cudaStream_t s) {
   if (nrows <= 0) return cudaSuccess;
+  if (fast::use_plane(nh, nw, row0, nrows)) {
+    fast::Args a{C, H, W, pad, nh, nw, row0, 0, BP, 1};
+    NOVA_PLANE_SWITCH(nh, nw, fast::launch_it_plane, x, V, a, nrows / nh,
+                      (unsigned)((C + 63) / 64), s);
+    return cudaGetLastError();
+  }
   const fast::Plan p = fast::make_plan(nw, C);
   fast::Args a{C, H, W, pad, nh, nw, row0, 0, BP, p.n_twc};
   const unsigned gx = (unsigned)(p.n_twc * p.n_cg);
@@ -312,6 +551,12 @@ cudaError_t launch_output_transform_fast(const __half* M, __half* y, int K, int 
                                          int nh, int nw, long long row0, long long nrows,
                                          long long BP, cudaStream_t s) {
   if (nrows <= 0) return cudaSuccess;
+  if (fast::use_plane(nh, nw, row0, nrows)) {
+    fast::Args a{K, H_out, W_out, 0, nh, nw, row0, 0, BP, 1};
+    NOVA_PLANE_SWITCH(nh, nw, fast::launch_ot_plane, M, y, a, nrows / nh,
+                      (unsigned)((K + 63) / 64), s);
+    return cudaGetLastError();
+  }
   const fast::Plan p = fast::make_plan(nw, K);
   fast::Args a{K, H_out, W_out, 0, nh, nw, row0, 0, BP, p.n_twc};
   const unsigned gx = (unsigned)(p.n_twc * p.n_cg);
