@@ -28,10 +28,15 @@ constexpr int kBM = 128;        // bp rows per tile
 constexpr int kBK = 64;         // input channels per stage (128 B of FP16)
 constexpr int kUmmaK = 16;      // K of one kind::f16 MMA
 constexpr int kMaxStages = 8;
-constexpr int kThreads = 192;   // 6 warps
-constexpr int kTmemCols = 512;
+constexpr int kThreads = 320;   // 10 warps: producer, MMA, 2 epilogue warpgroups
+#ifndef NOVA_GEMM_CTAS
+#define NOVA_GEMM_CTAS 1
+#endif
+constexpr int kCtasPerSm = NOVA_GEMM_CTAS;       // co-resident CTAs per SM
+constexpr int kTmemCols = 512 / kCtasPerSm;      // each CTA's TMEM share
+constexpr int kMaxBN = kTmemCols / 2 > 128 ? 128 : kTmemCols / 2;  // 2 accumulators
 constexpr unsigned long long kWaitLimitNs = 2000000000ull;  // 2 s per wait
-constexpr int kSmemLimit = 227 * 1024;
+constexpr int kSmemLimit = (227 * 1024) / kCtasPerSm - (kCtasPerSm > 1 ? 1024 : 0);
 
 struct Params {
   __half* M;
@@ -40,6 +45,7 @@ struct Params {
   int n_bp_tiles, n_k_tiles, n_cblk;
   long long total_tiles;
   int stages;
+  int tma_store;  // 1: epilogue stages 32-row slabs in smem and TMA-stores them
   int* status;
 };
 
@@ -105,6 +111,27 @@ __device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap* map
       " [%0], [%1, {%2, %3, %4}], [%5];" ::"r"(dst),
       "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(bar)
       : "memory");
+}
+
+__device__ __forceinline__ void tma_store_3d(const CUtensorMap* map, uint32_t src, int c0, int c1,
+                                             int c2) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.global.shared::cta.bulk_group [%0, {%1, %2, %3}], [%4];" ::"l"(
+          reinterpret_cast<uint64_t>(map)),
+      "r"(c0), "r"(c1), "r"(c2), "r"(src)
+      : "memory");
+}
+__device__ __forceinline__ void bulk_commit() {
+  asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+}
+__device__ __forceinline__ void bulk_wait_read_all() {
+  asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+}
+__device__ __forceinline__ void bulk_wait_all() {
+  asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+}
+__device__ __forceinline__ void fence_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
 
 // Shared-memory matrix descriptor: K-major operand, SWIZZLE_128B, 8-row atoms
@@ -182,9 +209,9 @@ __device__ __forceinline__ void store_row_f16(__half* dst, const uint32_t* r) {
   }
 }
 
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(kThreads, kCtasPerSm)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmU,
-                   const Params p) {
+                   const __grid_constant__ CUtensorMap tmM, const Params p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
@@ -192,7 +219,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t a_bytes = kBM * kBK * 2;
   const uint32_t b_bytes = (uint32_t)p.BN * kBK * 2;
   const uint32_t stage_bytes = a_bytes + b_bytes;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(base + (size_t)S * stage_bytes);
+  // Epilogue staging: one 32-row slab per epilogue warp, BN/64 chunks of
+  // 32 x 128 B in the SWIZZLE_128B layout the M tensor map stores from.
+  uint8_t* out_stage = base + (size_t)S * stage_bytes;
+  const uint32_t slab_bytes = p.tma_store ? 32u * (uint32_t)p.BN * 2u : 0u;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(out_stage + 8 * (size_t)slab_bytes);
   uint64_t* full = bars;
   uint64_t* empty = bars + kMaxStages;
   uint64_t* tfull = bars + 2 * kMaxStages;
@@ -298,11 +329,15 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     }
   } else {
-    // ---------------- Epilogue: warps 2..5 ----------------
+    // ---------------- Epilogue: warps 2..9 ----------------
+    // Warpgroup eg (warps 2-5 / 6-9) drains accumulator buffer eg, i.e. every
+    // other tile, so two tiles' epilogues proceed at once.
     const int q = warp & 3;  // TMEM lane quarter this warp may access
+    const int eg = (warp - 2) >> 2;
     const int row = q * 32 + lane;
-    uint32_t it = 0;
-    for (long long t = blockIdx.x; t < p.total_tiles; t += gridDim.x, ++it) {
+    uint32_t it = eg;
+    for (long long t = blockIdx.x + (long long)eg * gridDim.x; t < p.total_tiles;
+         t += 2ll * gridDim.x, it += 2) {
       const int pos = (int)(t / tiles_per_pos);
       const long long rem = t % tiles_per_pos;
       const int bpt = (int)(rem / p.n_k_tiles);
@@ -311,14 +346,50 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint32_t aph = (it >> 1) & 1u;
       if (!mbar_wait(smem_u32(&tfull[acc]), aph, abort_flag, p.status, kDevTimeoutEpilogue)) break;
       tc_fence_after();
+      const uint32_t taddr = tmem_base + ((uint32_t)(q * 32) << 16) + acc * (uint32_t)p.BN;
+      if (p.tma_store) {
+        uint8_t* slab = out_stage + (eg * 4 + q) * slab_bytes;
+        if (lane == 0) bulk_wait_read_all();  // the previous tile's store has read the slab
+        __syncwarp();
+        uint8_t* my_row = slab + lane * 128;
+        for (int j = 0; j < p.BN; j += 32) {
+          uint32_t r[32];
+          tmem_ld32(taddr + j, r);
+          uint8_t* chunk_row = my_row + (j >> 6) * 4096;
+          const int c_base = (j & 63) >> 3;  // first 16-byte chunk of these 32 columns
+#pragma unroll
+          for (int v = 0; v < 4; ++v) {
+            uint4 w;
+            w.x = pack_half2(r[8 * v + 0], r[8 * v + 1]);
+            w.y = pack_half2(r[8 * v + 2], r[8 * v + 3]);
+            w.z = pack_half2(r[8 * v + 4], r[8 * v + 5]);
+            w.w = pack_half2(r[8 * v + 6], r[8 * v + 7]);
+            *reinterpret_cast<uint4*>(chunk_row + (((c_base + v) ^ (lane & 7)) << 4)) = w;
+          }
+        }
+        tc_fence_before();
+        mbar_arrive(smem_u32(&tempty[acc]));  // TMEM is free once read
+        fence_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          for (int jc = 0; jc < p.BN / 64; ++jc)
+            tma_store_3d(&tmM, smem_u32(slab + jc * 4096), kt * p.BN + jc * 64,
+                         bpt * kBM + q * 32, pos);
+          bulk_commit();
+        }
+        continue;
+      }
       const long long bp = (long long)bpt * kBM + row;
       __half* out = p.M + ((long long)pos * p.BP + bp) * p.K + (long long)kt * p.BN;
-      const uint32_t taddr = tmem_base + ((uint32_t)(q * 32) << 16) + acc * (uint32_t)p.BN;
       int j = 0;
       for (; j + 32 <= p.BN; j += 32) {
         uint32_t r[32];
         tmem_ld32(taddr + j, r);
+#ifndef NOVA_GEMM_NO_STORE
         if (bp < p.BP) store_row_f16<4>(out + j, r);
+#else
+        if (bp < 0) store_row_f16<4>(out + j, r);
+#endif
       }
       if (j < p.BN) {  // BN is a multiple of 16: at most one 16-column tail
         uint32_t r[16];
@@ -328,6 +399,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_before();
       mbar_arrive(smem_u32(&tempty[acc]));
     }
+    if (p.tma_store && lane == 0) bulk_wait_all();  // stores complete before smem goes away
   }
 
   tc_fence_before();
@@ -378,7 +450,7 @@ static bool encode_operand_map(CUtensorMap* map, const void* ptr, int C, long lo
 }
 
 static int pick_bn(int K) {
-  for (int bn = 256; bn >= 16; bn -= 16)
+  for (int bn = kMaxBN; bn >= 16; bn -= 16)
     if (K % bn == 0) return bn;
   return 0;
 }
@@ -427,6 +499,9 @@ cudaError_t tc_gemm_run(const TcGemmPlan& plan, const __half* V, __half* M, long
     return cudaErrorInvalidValue;
   }
   tc::Params p;
+  CUtensorMap tmM;
+  p.tma_store = (plan.BN % 64) == 0 &&
+                tc::encode_operand_map(&tmM, M, plan.K, BP, 32);
   p.M = M;
   p.BP = BP;
   p.C = plan.C;
@@ -438,9 +513,13 @@ cudaError_t tc_gemm_run(const TcGemmPlan& plan, const __half* V, __half* M, long
   p.total_tiles = 64ll * p.n_bp_tiles * p.n_k_tiles;
   p.status = dev_status;
   const int stage_bytes = tc::kBM * tc::kBK * 2 + plan.BN * tc::kBK * 2;
-  const int overhead = 1024 + 256;
+  const int out_bytes = p.tma_store ? 8 * 32 * plan.BN * 2 : 0;
+  const int overhead = 1024 + 256 + out_bytes;
   p.stages = (tc::kSmemLimit - overhead) / stage_bytes;
   if (p.stages > tc::kMaxStages) p.stages = tc::kMaxStages;
+#ifdef NOVA_GEMM_STAGES
+  if (p.stages > NOVA_GEMM_STAGES) p.stages = NOVA_GEMM_STAGES;
+#endif
   const int smem = overhead + p.stages * stage_bytes;
   // The shared-memory opt-in is a per-device function attribute.
   static bool configured[64] = {};
@@ -456,8 +535,9 @@ cudaError_t tc_gemm_run(const TcGemmPlan& plan, const __half* V, __half* M, long
     }
     if (dev >= 0 && dev < 64) configured[dev] = true;
   }
-  long long grid = p.total_tiles < num_sms ? p.total_tiles : num_sms;
-  tc::gemm_tc_kernel<<<(unsigned)grid, tc::kThreads, smem, s>>>(tmV, plan.tmU, p);
+  const long long slots = (long long)num_sms * tc::kCtasPerSm;
+  long long grid = p.total_tiles < slots ? p.total_tiles : slots;
+  tc::gemm_tc_kernel<<<(unsigned)grid, tc::kThreads, smem, s>>>(tmV, plan.tmU, tmM, p);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) *why = "tensor-core GEMM launch failed";
   return e;
