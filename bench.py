@@ -486,6 +486,34 @@ def run_nova(args):
         dist.destroy_process_group()
 
 
+def profile_stages(args):
+    """Launch order: input transform, GEMM, output transform, repeated --steps
+    times, for one sweep layer at --batch (reference counterpart:
+    benchmarks/bench_profile_stages.py, which times the stages by subtraction)."""
+    import torch
+    from nova_winograd import ops
+    name, C, H = next(l for l in LAYERS if l[0] == args.profile_stages)
+    torch.cuda.set_device(0)
+    layers = build_layers(args.batch, torch.device("cuda", 0))
+    _, _, _, conv, x = next(l for l in layers if l[0] == name)
+    lib = ops.get_lib()
+    nt = live_tiles(H)
+    BP = args.batch * nt * nt
+    V = torch.empty(64, BP, C, dtype=torch.float16, device="cuda")
+    M = torch.empty(64, BP, C, dtype=torch.float16, device="cuda")
+    y = torch.empty(args.batch, C, H, H, dtype=torch.float16, device="cuda")
+    conv(x)
+    s = ops.stream_ptr()
+    for _ in range(args.steps):
+        ops.check(lib.nova_input_transform_v2(ops.ptr(x), ops.ptr(V), args.batch, C, H, H, 1,
+                                              nt, nt, BP, s), "input_transform")
+        ops.check(lib.nova_batched_gemm_v2(conv._handle, ops.ptr(V), ops.ptr(M), BP, s), "gemm")
+        ops.check(lib.nova_output_transform_v2(ops.ptr(M), ops.ptr(y), args.batch, C, H, H, nt,
+                                               nt, BP, s), "output_transform")
+    torch.cuda.synchronize()
+    print(f"profile-stages {name} batch {args.batch}: ok")
+
+
 def main():
     ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
     ap.add_argument("--gpus", type=int, default=1)
@@ -495,7 +523,13 @@ def main():
     ap.add_argument("--cpu-batch", type=int, default=1)
     ap.add_argument("--impl", choices=["nova", "reference"], default="nova")
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--profile-stages", metavar="LAYER", default=None,
+                    help="only run the three stage entries of one sweep layer (--steps times "
+                         "each, no timing output): the driver for ncu captures")
     args = ap.parse_args()
+    if args.profile_stages:
+        profile_stages(args)
+        return
     if args.impl == "reference":
         run_reference(args)
     else:
