@@ -241,7 +241,7 @@ int run_forward(Context* ctx, const void* x, void* y, void* V, void* M, int B, i
     const long long nrows = std::min(per_window, total_rows - r0);
     const long long BPw = nrows * nw;
     cudaError_t e =
-        even ? launch_input_transform_fast(xh, Vh, ctx->C, H, W, pad, nh, nw, r0, nrows, BPw, s)
+        even ? launch_input_transform_fast(xh, Vh, B, ctx->C, H, W, pad, nh, nw, r0, nrows, BPw, s)
              : launch_input_transform(xh, Vh, B, ctx->C, H, W, pad, nh, nw, BPw, s);
     if (e != cudaSuccess) return cuda_fail(ctx, e, "forward: input transform");
     if (path == 1) {

@@ -32,8 +32,8 @@ cudaError_t launch_output_transform(const __half* M, __half* y, int B, int K, in
 // Even channel counts: the fast kernels, over the tile rows [row0, row0+nrows)
 // (row = b*nh + th); inside V / M, bp = (row - row0)*nw + tw and BP is the
 // tensors' bp extent.
-cudaError_t launch_input_transform_fast(const __half* x, __half* V, int C, int H, int W, int pad,
-                                        int nh, int nw, long long row0, long long nrows,
+cudaError_t launch_input_transform_fast(const __half* x, __half* V, int B, int C, int H, int W,
+                                        int pad, int nh, int nw, long long row0, long long nrows,
                                         long long BP, cudaStream_t s);
 cudaError_t launch_output_transform_fast(const __half* M, __half* y, int K, int H_out, int W_out,
                                          int nh, int nw, long long row0, long long nrows,

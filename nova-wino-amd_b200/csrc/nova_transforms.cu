@@ -263,7 +263,7 @@ cudaError_t launch_filter_transform(const float* w, __half* U, int K, int C, boo
 cudaError_t launch_input_transform(const __half* x, __half* V, int B, int C, int H, int W,
                                    int pad, int nh, int nw, long long BP, cudaStream_t s) {
   if (C % 2 == 0)
-    return launch_input_transform_fast(x, V, C, H, W, pad, nh, nw, 0, (long long)B * nh, BP, s);
+    return launch_input_transform_fast(x, V, B, C, H, W, pad, nh, nw, 0, (long long)B * nh, BP, s);
   const int n_twc = (nw + kTW - 1) / kTW;
   const int n_cg = (C + kCG - 1) / kCG;
   dim3 grid(n_twc * n_cg, nh, B);

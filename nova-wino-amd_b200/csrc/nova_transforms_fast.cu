@@ -36,8 +36,22 @@ constexpr int kMaxTPC = 6;
 #endif
 constexpr long long kMaxGridY = 65535;
 
+// Dynamic shared memory above 48 KB is a per-device, per-kernel opt-in.
+template <const void* (*Fn)()>
+static bool smem_optin_once(size_t bytes) {
+  static bool done[64] = {};
+  if (bytes <= 48 * 1024) return true;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return false;
+  if (done[dev]) return true;
+  done[dev] = cudaFuncSetAttribute(Fn(), cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                   (int)bytes) == cudaSuccess;
+  return done[dev];
+}
+
 struct Args {
   int C, H, W, pad;  // C = channels of this tensor (C for input, K for output)
+  int B;             // batch
   int nh, nw;
   long long row0;    // first global tile row of the window
   long long lrow0;   // window-relative tile row of blockIdx.y == 0
@@ -54,7 +68,43 @@ struct Geo {
   static constexpr int kWarps = TPC * G < 2 ? 2 : TPC * G;
   static constexpr size_t kInSmem = 8 * kInCols * kPitch * 2;
   static constexpr size_t kOutSmem = 6 * kOutCols * kPitch * 2;
+  // TMA staging (W % 8 == 0): box {kBoxW, 8 rows, kCGN channels, 1 image}
+  // starting at the multiple of 8 at or below w0, landed as [c][r][w].
+  static constexpr int kBoxW = ((kInCols + 7 + 7) / 8) * 8;
+  static constexpr size_t kLandBytes = (size_t)kCGN * 8 * kBoxW * 2;
+  static constexpr size_t kInSmemTma = 128 + kLandBytes + kInSmem;
 };
+
+__device__ __forceinline__ void tma_load_4d(uint32_t dst, const CUtensorMap* map, int c0, int c1,
+                                            int c2, int c3, uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3, %4, %5}], [%6];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(bar)
+      : "memory");
+}
+
+// Bounded mbarrier wait (2 s of globaltimer); false on expiry.
+__device__ __forceinline__ bool mbar_wait_bounded(uint32_t bar, uint32_t parity) {
+  uint64_t t0 = 0;
+  for (uint32_t i = 0;; ++i) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(bar), "r"(parity)
+        : "memory");
+    if (ok) return true;
+    if ((i & 255u) == 0) {
+      uint64_t t;
+      asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+      if (t0 == 0) t0 = t;
+      else if (t - t0 > 2000000000ull) return false;
+    }
+  }
+}
 
 __device__ __forceinline__ void block_coords(const Args& a, long long& lrow, int& b, int& th,
                                              int& twc, int& cg) {
@@ -66,11 +116,18 @@ __device__ __forceinline__ void block_coords(const Args& a, long long& lrow, int
   th = (int)(grow - (long long)b * a.nh);
 }
 
-template <int TPC, int G>
+template <int TPC, int G, bool kTma>
 __global__ void __launch_bounds__(32 * Geo<TPC, G>::kWarps, NOVA_IT_MIN_BLOCKS)
-    input_transform_fast(const __half* __restrict__ x, __half* __restrict__ V, const Args a) {
+    input_transform_fast(const __half* __restrict__ x, __half* __restrict__ V,
+                         const __grid_constant__ CUtensorMap map_x, const Args a) {
   using Gm = Geo<TPC, G>;
-  __shared__ __align__(16) __half xs[8 * Gm::kInCols * Gm::kPitch];
+  extern __shared__ uint8_t it_raw[];
+  uint8_t* it_base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(it_raw) + 127) &
+                                                ~uintptr_t(127));
+  // TMA landing buffer [kCGN][8][kBoxW] (TMA path only), then [8][kInCols][kPitch].
+  const __half* land = reinterpret_cast<const __half*>(it_base);
+  __half* xs = reinterpret_cast<__half*>(it_base + (kTma ? Gm::kLandBytes : 0));
+  __shared__ uint64_t land_bar;
   long long lrow;
   int b, th, twc, cg;
   block_coords(a, lrow, b, th, twc, cg);
@@ -82,6 +139,37 @@ __global__ void __launch_bounds__(32 * Geo<TPC, G>::kWarps, NOVA_IT_MIN_BLOCKS)
   const int w0 = tw0 * 6 - a.pad;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
+  if constexpr (kTma) {
+    // One TMA tile load brings rows h0..h0+7, columns x0..x0+kBoxW-1 of the
+    // block's channels, zero-filled outside the tensor; then lanes (= columns)
+    // repack channel pairs into [row][col][channel].
+    const int x0 = w0 >= 0 ? (w0 & ~7) : -((-w0 + 7) & ~7);
+    const int d = w0 - x0;
+    const uint32_t bar = static_cast<uint32_t>(__cvta_generic_to_shared(&land_bar));
+    if (threadIdx.x == 0) {
+      asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(bar) : "memory");
+      asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar),
+                   "r"((uint32_t)Gm::kLandBytes)
+                   : "memory");
+      tma_load_4d(static_cast<uint32_t>(__cvta_generic_to_shared(land)), &map_x, x0, h0, c0, b,
+                  bar);
+    }
+    __syncthreads();
+    if (!mbar_wait_bounded(bar, 0)) return;
+    for (int q = warp; q < 8 * (Gm::kCGN / 2); q += Gm::kWarps) {
+      const int r = q & 7, p2 = q >> 3;  // row, channel pair
+      const __half* s0 = land + ((2 * p2) * 8 + r) * Gm::kBoxW + d;
+      const __half* s1 = s0 + 8 * Gm::kBoxW;
+      __half* dst = xs + r * Gm::kInCols * Gm::kPitch + 2 * p2;
+      if (lane < Gm::kInCols)
+        *reinterpret_cast<__half2*>(dst + lane * Gm::kPitch) = __halves2half2(s0[lane], s1[lane]);
+      if (lane + 32 < Gm::kInCols)
+        *reinterpret_cast<__half2*>(dst + (lane + 32) * Gm::kPitch) =
+            __halves2half2(s0[lane + 32], s1[lane + 32]);
+    }
+  } else {
   // Stage rows h0..h0+7 of the block's channels, columns w0..w0+kInCols-1.
   // A warp takes whole channels (kChanInFlight at a time: 16 loads per channel
   // per lane in flight); the 8 rows of a channel are one base pointer plus
@@ -128,6 +216,7 @@ __global__ void __launch_bounds__(32 * Geo<TPC, G>::kWarps, NOVA_IT_MIN_BLOCKS)
         }
       }
     }
+  }
   }
   __syncthreads();
 
@@ -420,19 +509,7 @@ __global__ void __launch_bounds__(32 * PlaneGeo<TR, TC>::kWarps, PlaneGeo<TR, TC
   }
 }
 
-// Shared memory above 48 KB is a per-device, per-kernel opt-in.
-template <const void* (*Fn)()>
-static bool smem_optin_once(size_t bytes) {
-  static bool done[64] = {};
-  if (bytes <= 48 * 1024) return true;
-  int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return false;
-  if (done[dev]) return true;
-  done[dev] = cudaFuncSetAttribute(Fn(), cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                   (int)bytes) == cudaSuccess;
-  return done[dev];
-}
-
+// Kernel addresses for the shared-memory opt-in.
 template <int TR, int TC>
 const void* it_plane_fn() { return (const void*)input_transform_plane<TR, TC>; }
 template <int TR, int TC>
@@ -496,13 +573,59 @@ static Plan make_plan(int nw, int C) {
   return p;
 }
 
+
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                   const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                   const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                   CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      return reinterpret_cast<EncodeTiledFn>(p);
+    return static_cast<EncodeTiledFn>(nullptr);
+  }();
+  return fn;
+}
+
+// 4-D map over x [B][C][H][W] (W fastest) with box {box_w, 8, cgn, 1}; needs
+// W % 8 == 0 (16-byte row stride) and a 16-byte aligned base.
+static bool encode_x_map(CUtensorMap* map, const __half* x, int B, int C, int H, int W,
+                         int box_w, int cgn) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn || (W % 8) || (reinterpret_cast<uintptr_t>(x) & 15)) return false;
+  cuuint64_t dims[4] = {(cuuint64_t)W, (cuuint64_t)H, (cuuint64_t)C, (cuuint64_t)B};
+  cuuint64_t strides[3] = {(cuuint64_t)W * 2, (cuuint64_t)H * W * 2, (cuuint64_t)C * H * W * 2};
+  cuuint32_t box[4] = {(cuuint32_t)box_w, 8, (cuuint32_t)cgn, 1};
+  cuuint32_t estr[4] = {1, 1, 1, 1};
+  return fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4, const_cast<__half*>(x), dims, strides, box,
+            estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+            CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+template <int TPC, int G>
+const void* it_tma_fn() { return (const void*)input_transform_fast<TPC, G, true>; }
+
 template <int TPC, int G>
 static void launch_it(const __half* x, __half* V, Args a, long long nrows, unsigned gx,
                       cudaStream_t s) {
+  using Gm = Geo<TPC, G>;
+  CUtensorMap map{};
+  const bool tma = encode_x_map(&map, x, a.B, a.C, a.H, a.W, Gm::kBoxW, Gm::kCGN) &&
+                   smem_optin_once<it_tma_fn<TPC, G>>(Gm::kInSmemTma);
   for (long long done = 0; done < nrows; done += kMaxGridY) {
     a.lrow0 = done;
     dim3 grid(gx, (unsigned)std::min(kMaxGridY, nrows - done));
-    input_transform_fast<TPC, G><<<grid, 32 * Geo<TPC, G>::kWarps, 0, s>>>(x, V, a);
+    if (tma)
+      input_transform_fast<TPC, G, true><<<grid, 32 * Gm::kWarps, Gm::kInSmemTma, s>>>(x, V, map,
+                                                                                     a);
+    else
+      input_transform_fast<TPC, G, false><<<grid, 32 * Gm::kWarps, Gm::kInSmem + 128, s>>>(
+          x, V, map, a);
   }
 }
 
@@ -530,18 +653,18 @@ static void launch_ot(const __half* M, __half* y, Args a, long long nrows, unsig
 
 }  // namespace fast
 
-cudaError_t launch_input_transform_fast(const __half* x, __half* V, int C, int H, int W, int pad,
-                                        int nh, int nw, long long row0, long long nrows,
+cudaError_t launch_input_transform_fast(const __half* x, __half* V, int B, int C, int H, int W,
+                                        int pad, int nh, int nw, long long row0, long long nrows,
                                         long long BP, cudaStream_t s) {
   if (nrows <= 0) return cudaSuccess;
   if (fast::use_plane(nh, nw, row0, nrows)) {
-    fast::Args a{C, H, W, pad, nh, nw, row0, 0, BP, 1};
+    fast::Args a{C, H, W, pad, B, nh, nw, row0, 0, BP, 1};
     NOVA_PLANE_SWITCH(nh, nw, fast::launch_it_plane, x, V, a, nrows / nh,
                       (unsigned)((C + 63) / 64), s);
     return cudaGetLastError();
   }
   const fast::Plan p = fast::make_plan(nw, C);
-  fast::Args a{C, H, W, pad, nh, nw, row0, 0, BP, p.n_twc};
+  fast::Args a{C, H, W, pad, B, nh, nw, row0, 0, BP, p.n_twc};
   const unsigned gx = (unsigned)(p.n_twc * p.n_cg);
   NOVA_TPC_SWITCH(p.tpc, p.G, fast::launch_it, x, V, a, nrows, gx, s);
   return cudaGetLastError();
@@ -552,13 +675,13 @@ cudaError_t launch_output_transform_fast(const __half* M, __half* y, int K, int 
                                          long long BP, cudaStream_t s) {
   if (nrows <= 0) return cudaSuccess;
   if (fast::use_plane(nh, nw, row0, nrows)) {
-    fast::Args a{K, H_out, W_out, 0, nh, nw, row0, 0, BP, 1};
+    fast::Args a{K, H_out, W_out, 0, 0, nh, nw, row0, 0, BP, 1};
     NOVA_PLANE_SWITCH(nh, nw, fast::launch_ot_plane, M, y, a, nrows / nh,
                       (unsigned)((K + 63) / 64), s);
     return cudaGetLastError();
   }
   const fast::Plan p = fast::make_plan(nw, K);
-  fast::Args a{K, H_out, W_out, 0, nh, nw, row0, 0, BP, p.n_twc};
+  fast::Args a{K, H_out, W_out, 0, 0, nh, nw, row0, 0, BP, p.n_twc};
   const unsigned gx = (unsigned)(p.n_twc * p.n_cg);
   NOVA_TPC_SWITCH(p.tpc, p.G, fast::launch_ot, M, y, a, nrows, gx, s);
   return cudaGetLastError();
