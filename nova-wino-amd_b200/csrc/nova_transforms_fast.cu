@@ -351,7 +351,11 @@ struct PlaneGeo {
   static constexpr int kOutCells = 36 * TR * TC;
   static constexpr int kOutPerLane = (kOutCells + 31) / 32;
   static constexpr int kPitch = 66;                                // 64 channels + 2
-  static constexpr int kWarps = TR * TC < 2 ? 2 : TR * TC;
+#ifndef NOVA_PLANE_MAX_WARPS
+#define NOVA_PLANE_MAX_WARPS 5  // measured: 3x3-tile images run best at 5 warps, 3 blocks/SM
+#endif
+  static constexpr int kWarps =
+      TR * TC < 2 ? 2 : (TR * TC > NOVA_PLANE_MAX_WARPS ? NOVA_PLANE_MAX_WARPS : TR * TC);
   // Blocks per SM the register budget is sized for (about 128 registers/thread).
   static constexpr int kMinBlocks = 65536 / (128 * 32 * kWarps) < 1 ? 1 : 65536 / (128 * 32 * kWarps);
   static constexpr size_t kInSmem = (size_t)kCells * kPitch * 2;
