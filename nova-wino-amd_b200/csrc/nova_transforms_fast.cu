@@ -116,7 +116,10 @@ __device__ __forceinline__ void block_coords(const Args& a, long long& lrow, int
   th = (int)(grow - (long long)b * a.nh);
 }
 
-template <int TPC, int G, bool kTma>
+// kMode: 0 = staged with plain loads; 1 = one TMA tile load of 8 image rows
+// (W % 8 == 0); 2 = one TMA tile load of 5 "pair rows" (2 image rows each, for
+// W % 4 == 0 and even H, where single rows are not 16-byte strided).
+template <int TPC, int G, int kMode>
 __global__ void __launch_bounds__(32 * Geo<TPC, G>::kWarps, NOVA_IT_MIN_BLOCKS)
     input_transform_fast(const __half* __restrict__ x, __half* __restrict__ V,
                          const __grid_constant__ CUtensorMap map_x, const Args a) {
@@ -126,7 +129,10 @@ __global__ void __launch_bounds__(32 * Geo<TPC, G>::kWarps, NOVA_IT_MIN_BLOCKS)
                                                 ~uintptr_t(127));
   // TMA landing buffer [kCGN][8][kBoxW] (TMA path only), then [8][kInCols][kPitch].
   const __half* land = reinterpret_cast<const __half*>(it_base);
-  __half* xs = reinterpret_cast<__half*>(it_base + (kTma ? Gm::kLandBytes : 0));
+  const size_t land_bytes =
+      kMode == 1 ? Gm::kLandBytes
+                 : (kMode == 2 ? (((size_t)Gm::kCGN * 5 * 2 * a.W * 2 + 127) / 128) * 128 : 0);
+  __half* xs = reinterpret_cast<__half*>(it_base + land_bytes);
   __shared__ uint64_t land_bar;
   long long lrow;
   int b, th, twc, cg;
@@ -139,7 +145,42 @@ __global__ void __launch_bounds__(32 * Geo<TPC, G>::kWarps, NOVA_IT_MIN_BLOCKS)
   const int w0 = tw0 * 6 - a.pad;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
-  if constexpr (kTma) {
+  if constexpr (kMode == 2) {
+    // Pair rows: row pr of the landing buffer holds image rows 2(p0+pr) and
+    // 2(p0+pr)+1 back to back (2W halves), zero-filled outside the tensor.
+    const int p0 = h0 >= 0 ? h0 / 2 : -((-h0 + 1) / 2);
+    const int W2 = 2 * W;
+    const uint32_t bar = static_cast<uint32_t>(__cvta_generic_to_shared(&land_bar));
+    if (threadIdx.x == 0) {
+      asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(bar) : "memory");
+      asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar),
+                   "r"((uint32_t)(Gm::kCGN * 5 * W2 * 2))
+                   : "memory");
+      tma_load_4d(static_cast<uint32_t>(__cvta_generic_to_shared(land)), &map_x, 0, p0, c0, b,
+                  bar);
+    }
+    __syncthreads();
+    if (!mbar_wait_bounded(bar, 0)) return;
+    const bool ok0 = lane < Gm::kInCols && w0 + lane >= 0 && w0 + lane < W;
+    const bool ok1 = lane + 32 < Gm::kInCols && w0 + lane + 32 >= 0 && w0 + lane + 32 < W;
+    for (int q = warp; q < 8 * (Gm::kCGN / 2); q += Gm::kWarps) {
+      const int r = q & 7, p2 = q >> 3;
+      const int h = h0 + r;
+      const int hp = h >= 0 ? h / 2 : -((-h + 1) / 2);
+      const __half* s0 = land + ((2 * p2) * 5 + (hp - p0)) * W2 + (h - 2 * hp) * W + w0;
+      const __half* s1 = s0 + 5 * W2;
+      __half* dst = xs + r * Gm::kInCols * Gm::kPitch + 2 * p2;
+      const __half z = __ushort_as_half(0);
+      if (lane < Gm::kInCols)
+        *reinterpret_cast<__half2*>(dst + lane * Gm::kPitch) =
+            ok0 ? __halves2half2(s0[lane], s1[lane]) : __halves2half2(z, z);
+      if (lane + 32 < Gm::kInCols)
+        *reinterpret_cast<__half2*>(dst + (lane + 32) * Gm::kPitch) =
+            ok1 ? __halves2half2(s0[lane + 32], s1[lane + 32]) : __halves2half2(z, z);
+    }
+  } else if constexpr (kMode == 1) {
     // One TMA tile load brings rows h0..h0+7, columns x0..x0+kBoxW-1 of the
     // block's channels, zero-filled outside the tensor; then lanes (= columns)
     // repack channel pairs into [row][col][channel].
@@ -612,24 +653,58 @@ static bool encode_x_map(CUtensorMap* map, const __half* x, int B, int C, int H,
 }
 
 template <int TPC, int G>
-const void* it_tma_fn() { return (const void*)input_transform_fast<TPC, G, true>; }
+const void* it_tma_fn() { return (const void*)input_transform_fast<TPC, G, 1>; }
+template <int TPC, int G>
+const void* it_pair_fn() { return (const void*)input_transform_fast<TPC, G, 2>; }
+
+constexpr size_t kPairSmemMax = 100 * 1024;
+
+// Pair-row view of x: dims {2W, H/2, C, B}, box {2W, 5, cgn, 1}.
+static bool encode_x_pair_map(CUtensorMap* map, const __half* x, int B, int C, int H, int W,
+                              int cgn) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn || (W % 4) || (H % 2) || 2 * W > 256 || (reinterpret_cast<uintptr_t>(x) & 15))
+    return false;
+  cuuint64_t dims[4] = {(cuuint64_t)2 * W, (cuuint64_t)H / 2, (cuuint64_t)C, (cuuint64_t)B};
+  cuuint64_t strides[3] = {(cuuint64_t)W * 4, (cuuint64_t)H * W * 2, (cuuint64_t)C * H * W * 2};
+  cuuint32_t box[4] = {(cuuint32_t)(2 * W), 5, (cuuint32_t)cgn, 1};
+  cuuint32_t estr[4] = {1, 1, 1, 1};
+  return fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4, const_cast<__half*>(x), dims, strides, box,
+            estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+            CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
 
 template <int TPC, int G>
 static void launch_it(const __half* x, __half* V, Args a, long long nrows, unsigned gx,
                       cudaStream_t s) {
   using Gm = Geo<TPC, G>;
   CUtensorMap map{};
-  const bool tma = encode_x_map(&map, x, a.B, a.C, a.H, a.W, Gm::kBoxW, Gm::kCGN) &&
-                   smem_optin_once<it_tma_fn<TPC, G>>(Gm::kInSmemTma);
+  int mode = 0;
+  size_t smem = Gm::kInSmem + 128;
+  if (encode_x_map(&map, x, a.B, a.C, a.H, a.W, Gm::kBoxW, Gm::kCGN) &&
+      smem_optin_once<it_tma_fn<TPC, G>>(Gm::kInSmemTma)) {
+    mode = 1;
+    smem = Gm::kInSmemTma;
+  } else {
+    const size_t pair_smem =
+        128 + (((size_t)Gm::kCGN * 5 * 2 * a.W * 2 + 127) / 128) * 128 + Gm::kInSmem;
+    if (pair_smem <= kPairSmemMax &&
+        encode_x_pair_map(&map, x, a.B, a.C, a.H, a.W, Gm::kCGN) &&
+        smem_optin_once<it_pair_fn<TPC, G>>(kPairSmemMax)) {
+      mode = 2;
+      smem = pair_smem;
+    }
+  }
   for (long long done = 0; done < nrows; done += kMaxGridY) {
     a.lrow0 = done;
     dim3 grid(gx, (unsigned)std::min(kMaxGridY, nrows - done));
-    if (tma)
-      input_transform_fast<TPC, G, true><<<grid, 32 * Gm::kWarps, Gm::kInSmemTma, s>>>(x, V, map,
-                                                                                     a);
+    const unsigned thr = 32 * Gm::kWarps;
+    if (mode == 1)
+      input_transform_fast<TPC, G, 1><<<grid, thr, smem, s>>>(x, V, map, a);
+    else if (mode == 2)
+      input_transform_fast<TPC, G, 2><<<grid, thr, smem, s>>>(x, V, map, a);
     else
-      input_transform_fast<TPC, G, false><<<grid, 32 * Gm::kWarps, Gm::kInSmem + 128, s>>>(
-          x, V, map, a);
+      input_transform_fast<TPC, G, 0><<<grid, thr, smem, s>>>(x, V, map, a);
   }
 }
 
