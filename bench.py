@@ -144,7 +144,7 @@ def run_reference(args):
         "note": "reference is HIP/rocBLAS for MI300X and cannot run here; its NOVA math is "
                 "timed as the numpy restatement (oracle/nova_oracle.py) on the host cores",
     }
-    print(json.dumps(line), flush=True)
+    emit(line)
 
 
 # ---------------------------------------------------------------------------
@@ -217,14 +217,17 @@ def barrier(dist):
     import torch
     if dist is not None:
         dist.barrier()
-    torch.cuda.synchronize()
+    if torch.cuda.is_available():
+        torch.cuda.synchronize()
 
 
 def max_over_ranks(dist, value):
+    """Max of a per-rank time over all ranks (NCCL tensors on the GPU, gloo on CPU)."""
     import torch
     if dist is None:
         return value
-    t = torch.tensor([value], dtype=torch.float64, device="cuda")
+    dev = "cuda" if dist.get_backend() == "nccl" else "cpu"
+    t = torch.tensor([value], dtype=torch.float64, device=dev)
     dist.all_reduce(t, op=dist.ReduceOp.MAX)
     return float(t.item())
 
@@ -262,8 +265,10 @@ def make_flush(device):
 
 
 def time_kernel(fn, reps, flush):
-    """Average device time (ms) of fn() with an L2 flush between launches."""
+    """Median device time (ms) of fn() with an L2 flush before each launch
+    (one untimed call first)."""
     import torch
+    fn()
     evs = []
     for _ in range(reps):
         flush()
@@ -273,7 +278,7 @@ def time_kernel(fn, reps, flush):
         e.record()
         evs.append((s, e))
     torch.cuda.synchronize()
-    return sum(s.elapsed_time(e) for s, e in evs) / reps
+    return statistics.median(s.elapsed_time(e) for s, e in evs)
 
 
 def stage_profile(layers, batch, flush, reps=10):
@@ -317,6 +322,29 @@ def stage_profile(layers, batch, flush, reps=10):
                         "flops": flops, "gbs": nbytes / ms / 1e6,
                         "tflops": flops / ms / 1e9 if flops else None})
     return out
+
+
+def vendor_layer_times(layers, flush, reps=10):
+    """Whole-layer device time of our forward and of torch's FP16 conv2d (cuDNN)
+    on the same layer, L2 flushed before each launch (context, like the
+    reference's MIOpen comparison in benchmarks/bench_layers.py)."""
+    import torch
+    import torch.nn.functional as F
+    res = {}
+    torch.backends.cudnn.benchmark = True
+    for name, C, H, conv, x in layers:
+        w16 = conv.weight.detach().half()
+        with torch.no_grad():
+            for _ in range(3):  # cuDNN algorithm selection happens here
+                F.conv2d(x, w16, padding=1)
+        with torch.no_grad():
+            ours = time_kernel(lambda: conv(x), reps, flush)
+            cudnn = time_kernel(lambda: F.conv2d(x, w16, padding=1), reps, flush)
+        fl = direct_flops(x.shape[0], C, C, H)
+        res[name] = {"nova_us": round(ours * 1e3, 1), "cudnn_fp16_us": round(cudnn * 1e3, 1),
+                     "nova_eff_tflops": round(fl / ours / 1e9, 1),
+                     "cudnn_eff_tflops": round(fl / cudnn / 1e9, 1)}
+    return res
 
 
 def roofline_from_stages(stages, peaks):
@@ -450,11 +478,12 @@ def run_nova(args):
     e2e_ms = max_over_ranks(dist, s.elapsed_time(e))
     e2e_value = world * flops_step * args.steps / (e2e_ms / 1e3) / 1e12
 
-    stages = roofline = lat = cpu = None
+    stages = roofline = lat = cpu = vendor = None
     if rank == 0:
         stages = stage_profile(layers, batch, flush)
         roofline = roofline_from_stages(stages, peaks)
         lat = b1_latency(device)
+        vendor = vendor_layer_times(layers, flush)
         if world == 1 and not args.no_cpu:
             v, threads, sample, extra = cpu_nova_sample(args.cpu_batch)
             cpu = {"value": v, "unit": UNIT, "cores": threads, "kind": "port", "sample": sample}
@@ -478,10 +507,86 @@ def run_nova(args):
             "stages": [{k: (round(v, 5) if isinstance(v, float) else v) for k, v in st.items()}
                        for st in stages],
             "b1_latency_us": lat,
+            "per_layer_vs_cudnn": vendor,
             "step_ms": [round(t, 4) for t in step_ms],
             "library": ops.get_lib().nova_version().decode(),
         }
-        print(json.dumps(line), flush=True)
+        emit(line)
+    if dist is not None:
+        dist.destroy_process_group()
+
+
+def run_resnet50(args):
+    """torchvision ResNet-50 (random init, BN in eval mode
+    with running mean 0 / var 1), FP16, 3x224x224 N(0,1) input; the 13 eligible
+    3x3 stride-1 convs replaced by replace_conv2d_with_nova.  Data parallel by
+    batch: every rank runs --batch images per step (weak scaling).  The same
+    model without replacement (cuDNN) is timed alongside for context."""
+    import torch
+    import torchvision
+    from nova_winograd import replace_conv2d_with_nova
+    world, rank, local, dist = setup_dist()
+    device = torch.device("cuda", local)
+    torch.manual_seed(1234 + rank)
+    ref = torchvision.models.resnet50().to(device).half().eval()
+    model = torchvision.models.resnet50().to(device).half().eval()
+    model.load_state_dict(ref.state_dict())
+    n_rep = replace_conv2d_with_nova(model, verbose=False)
+    x = torch.randn(args.batch, 3, 224, 224, device=device, dtype=torch.float16)
+
+    def timed(m, steps, warmup):
+        with torch.no_grad():
+            for _ in range(warmup):
+                out = m(x)
+            barrier(dist)
+            s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            s.record()
+            for _ in range(steps):
+                out = m(x)
+            e.record()
+            torch.cuda.synchronize()
+        return max_over_ranks(dist, s.elapsed_time(e)), out
+
+    uuid = str(torch.cuda.get_device_properties(device).uuid)
+    sampler = ClockSampler(uuid if uuid.startswith("GPU-") else f"GPU-{uuid}")
+    sampler.start()
+    ms, out = timed(model, args.steps, args.warmup)
+    clocks = sampler.stop()
+    ms_ref, out_ref = timed(ref, args.steps, args.warmup)
+    value = world * args.batch * args.steps / (ms / 1e3)
+    finite = bool(torch.isfinite(out).all().item())
+    rel = float(((out.float() - out_ref.float()).norm() / out_ref.float().norm()).item())
+    # End to end: pinned host images in, logits out, every step.
+    hx = x.cpu().pin_memory()
+    hy = torch.empty(args.batch, 1000, dtype=torch.float16).pin_memory()
+    with torch.no_grad():
+        for _ in range(max(1, args.warmup)):
+            hy.copy_(model(hx.to(device, non_blocking=True)), non_blocking=True)
+        barrier(dist)
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        for _ in range(args.steps):
+            hy.copy_(model(hx.to(device, non_blocking=True)), non_blocking=True)
+        e.record()
+        torch.cuda.synchronize()
+    e2e_ms = max_over_ranks(dist, s.elapsed_time(e))
+    if rank == 0:
+        emit({
+            "metric": "ResNet-50 FP16 inference images/s (13 3x3 s1 convs on NOVA F(6,3))",
+            "value": value, "unit": "img/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f16",
+            "data": "synthetic (N(0,1) images, random-init weights, BN eval mean 0 / var 1)",
+            "config": {"workload": "resnet50", "batch_per_gpu": args.batch,
+                       "parallelism": f"dp{world} (batch-partitioned)", "replaced_convs": n_rep,
+                       "l2": "activations far larger than L2"},
+            "e2e": {"value": world * args.batch * args.steps / (e2e_ms / 1e3), "unit": "img/s",
+                    "h2d_bytes_per_step": hx.numel() * 2, "d2h_bytes_per_step": hy.numel() * 2},
+            "gpu_launches": 3 * n_rep * args.steps,
+            "cudnn_same_model_img_s": world * args.batch * args.steps / (ms_ref / 1e3),
+            "logits_finite": finite, "logits_rel_diff_vs_cudnn": rel,
+            "clocks": clocks,
+        })
     if dist is not None:
         dist.destroy_process_group()
 
@@ -514,7 +619,22 @@ def profile_stages(args):
     print(f"profile-stages {name} batch {args.batch}: ok")
 
 
+_JSON_OUT = None
+
+
+def emit(line):
+    """The one JSON line on the original stdout; everything else (libraries
+    included, e.g. NCCL's version banner) goes to stderr."""
+    out = _JSON_OUT or sys.stdout
+    out.write(json.dumps(line) + "\n")
+    out.flush()
+
+
 def main():
+    global _JSON_OUT
+    sys.stdout.flush()
+    _JSON_OUT = os.fdopen(os.dup(1), "w")
+    os.dup2(2, 1)
     ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=20)
@@ -523,6 +643,9 @@ def main():
     ap.add_argument("--cpu-batch", type=int, default=1)
     ap.add_argument("--impl", choices=["nova", "reference"], default="nova")
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--workload", choices=["sweep", "resnet50"], default="sweep",
+                    help="sweep: ResNet-50 3x3 layer sweep (BASELINE config 2, default); "
+                         "resnet50: whole model images/s (config 3)")
     ap.add_argument("--profile-stages", metavar="LAYER", default=None,
                     help="only run the three stage entries of one sweep layer (--steps times "
                          "each, no timing output): the driver for ncu captures")
@@ -532,6 +655,9 @@ def main():
         return
     if args.impl == "reference":
         run_reference(args)
+    elif args.workload == "resnet50":
+        args.warmup = max(3, args.warmup)
+        run_resnet50(args)
     else:
         args.warmup = max(3, args.warmup)
         run_nova(args)
