@@ -125,8 +125,12 @@ int nova_batched_gemm_v2(nova_handle_t h, const void* d_V_gemm, void* d_M_gemm, 
 long long nova_workspace_bytes(nova_handle_t h, int batch, int H, int W, int pad);
 
 /* Path selection.  0 = automatic dispatch, 1 = 3-pass with the tcgen05 GEMM,
- * 2 = 3-pass with the SIMT GEMM.  Returns NOVA_ERR_INVALID_ARGUMENT for a path
- * the current weights cannot take.  nova_get_path reports the path the last
+ * 2 = 3-pass with the SIMT GEMM, 3 = the fused single kernel (transform ->
+ * tcgen05 MMA -> inverse, no V/M in HBM; C in {16, 32, 48, 64} and K <= 64,
+ * the fused path of csrc/nova_winograd_fused.hip:511).  The automatic dispatch
+ * takes the fused kernel for those shapes up to a live-tile count and the
+ * tcgen05 3-pass beyond it.  Stage entries (nova_batched_gemm_v2) treat 3 as 1.
+ * Returns NOVA_ERR_INVALID_ARGUMENT for a path the current weights cannot take.  nova_get_path reports the path the last
  * forward on this handle ran. */
 int nova_set_path(nova_handle_t h, int path);
 int nova_get_path(nova_handle_t h);

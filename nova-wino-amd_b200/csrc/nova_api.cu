@@ -40,6 +40,10 @@ __global__ void u_to_ref_layout_kernel(const __half* __restrict__ Uint, __half* 
 
 namespace {
 
+// 0 until the fused kernel beats the 3-pass path at some batch (it is opt-in via
+// nova_set_path(h, 3) meanwhile).
+constexpr long long kFusedMaxBpDefault = 0;
+
 thread_local std::string t_err_msg = "no error";
 thread_local int t_err_code = NOVA_OK;
 
@@ -54,6 +58,8 @@ struct Context {
   bool U_ref_valid = false;
   TcGemmPlan plan;
   bool tc_ok = false;
+  FusedPlan fplan;
+  bool fused_ok = false;
   void* ws = nullptr;
   size_t ws_bytes = 0;
   int* d_status = nullptr;
@@ -171,6 +177,11 @@ int set_weights(Context* ctx, const void* w, int K, int C, cudaStream_t s) {
     const char* why = nullptr;
     ctx->tc_ok = tc_gemm_plan(&ctx->plan, ctx->U, K, C, &why) == cudaSuccess;
   }
+  ctx->fused_ok = false;
+  if (fused_supported(C, K)) {
+    const char* why = nullptr;
+    ctx->fused_ok = fused_plan(&ctx->fplan, ctx->U, K, C, &why) == cudaSuccess;
+  }
   ctx->has_weights = true;
   return ok(ctx);
 }
@@ -187,8 +198,23 @@ int check_forward_args(Context* ctx, const void* x, const void* y, int B, int H,
   return NOVA_OK;
 }
 
-int choose_path(Context* ctx) {
-  if (ctx->forced_path == 1 || (ctx->forced_path == 0 && ctx->tc_ok)) return 1;
+// Largest live-tile count BP = B*ceil(H_out/6)*ceil(W_out/6) for which the
+// automatic dispatch runs the fused kernel (NOVA_FUSED_MAX_BP overrides).
+long long fused_max_bp() {
+  static const long long v = [] {
+    const char* env = std::getenv("NOVA_FUSED_MAX_BP");
+    return env ? std::atoll(env) : kFusedMaxBpDefault;
+  }();
+  return v;
+}
+
+// Path ids: 1 = 3-pass with the tcgen05 GEMM, 2 = 3-pass with the SIMT GEMM,
+// 3 = fused single kernel.  BP < 0 asks for a GEMM-only path.
+int choose_path(Context* ctx, long long BP = -1) {
+  if (ctx->forced_path == 3 && BP >= 0) return 3;
+  if (ctx->forced_path == 0 && BP >= 0 && ctx->fused_ok && BP <= fused_max_bp()) return 3;
+  if (ctx->forced_path == 1 || ctx->forced_path == 3 || (ctx->forced_path == 0 && ctx->tc_ok))
+    return ctx->tc_ok ? 1 : 2;
   return 2;
 }
 
@@ -233,7 +259,14 @@ int run_forward(Context* ctx, const void* x, void* y, void* V, void* M, int B, i
   __half* Vh = static_cast<__half*>(V);
   __half* Mh = static_cast<__half*>(M);
   __half* yh = static_cast<__half*>(y);
-  const int path = choose_path(ctx);
+  const int path = choose_path(ctx, (long long)B * nh * nw);
+  if (path == 3) {
+    const char* why = "";
+    cudaError_t e = fused_run(ctx->fplan, xh, yh, B, H, W, pad, ctx->d_status, s, &why);
+    if (e != cudaSuccess) return fail(ctx, NOVA_ERR_CUDA, std::string("forward: fused: ") + why);
+    ctx->last_path = 3;
+    return ok(ctx);
+  }
   const bool even = ctx->C % 2 == 0 && ctx->K % 2 == 0;
   const long long total_rows = (long long)B * nh;
   const long long per_window = even ? window_rows(ctx, nw, total_rows) : total_rows;
@@ -514,8 +547,11 @@ NOVA_EXPORT long long nova_workspace_bytes(nova_handle_t h, int batch, int H, in
 NOVA_EXPORT int nova_set_path(nova_handle_t h, int path) {
   Context* ctx = as_ctx(h);
   if (!ctx) return nova::fail(nullptr, NOVA_ERR_INVALID_ARGUMENT, "set_path: null handle");
-  if (path < 0 || path > 2)
+  if (path < 0 || path > 3)
     return nova::fail(ctx, NOVA_ERR_INVALID_ARGUMENT, "set_path: unknown path");
+  if (path == 3 && !ctx->fused_ok)
+    return nova::fail(ctx, NOVA_ERR_INVALID_ARGUMENT,
+                      "set_path: fused kernel needs C in {16, 32, 48, 64} and K <= 64");
   if (path == 1 && !ctx->tc_ok)
     return nova::fail(ctx, NOVA_ERR_INVALID_ARGUMENT,
                       "set_path: tcgen05 GEMM needs C % 8 == 0 and K % 16 == 0");

@@ -21,6 +21,7 @@ enum DeviceStatus : int {
   kDevTimeoutProducer = 1,  // TMA producer gave up waiting for a free stage
   kDevTimeoutMma = 2,       // MMA issuer gave up waiting for operands / accumulator
   kDevTimeoutEpilogue = 3,  // epilogue gave up waiting for an accumulator
+  kDevTimeoutFused = 4,     // fused kernel gave up waiting for U or its MMAs
 };
 
 cudaError_t launch_filter_transform(const float* w, __half* U, int K, int C, bool ref_layout,
@@ -56,5 +57,24 @@ cudaError_t tc_gemm_plan(TcGemmPlan* plan, const __half* U, int K, int C, const 
 // M[pos][bp][k] = sum_c V[pos][bp][c] U[pos][k][c] on the tensor cores.
 cudaError_t tc_gemm_run(const TcGemmPlan& plan, const __half* V, __half* M, long long BP,
                         int* dev_status, int num_sms, cudaStream_t s, const char** why);
+
+// 3-D FP16 tensor map over [64][rows][C] (C fastest), box {64, box_rows, 1},
+// SWIZZLE_128B: the layout of the UMMA K-major operands.
+bool tc_encode_operand_map(CUtensorMap* map, const void* ptr, int C, long long rows,
+                           int box_rows);
+
+// Single-kernel forward (transform -> tcgen05 MMA -> inverse) for C, K <= 64.
+struct FusedPlan {
+  CUtensorMap tmU;  // U internal layout [64][K][C], box {64 c, 64 k, 1}
+  int K = 0, C = 0;
+  bool valid = false;
+};
+
+// True when (C, K) is a shape the fused kernel takes: C in {16, 32, 48, 64}, K <= 64.
+bool fused_supported(int C, int K);
+cudaError_t fused_plan(FusedPlan* plan, const __half* U, int K, int C, const char** why);
+// y = conv(x) for the whole batch; no workspace.
+cudaError_t fused_run(const FusedPlan& plan, const __half* x, __half* y, int B, int H, int W,
+                      int pad, int* dev_status, cudaStream_t s, const char** why);
 
 }  // namespace nova

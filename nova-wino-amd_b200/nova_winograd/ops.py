@@ -64,7 +64,7 @@ SIGNATURES = {
 }
 
 # Path ids of nova_set_path / nova_get_path.
-PATH_AUTO, PATH_TCGEN05, PATH_SIMT = 0, 1, 2
+PATH_AUTO, PATH_TCGEN05, PATH_SIMT, PATH_FUSED = 0, 1, 2, 3
 
 
 def lib_path_candidates():

@@ -100,9 +100,59 @@ PARITY_CASES = [
 def test_forward_parity_auto(B, C, K, H, W, pad):
     x, w = o.synthetic_case(B, C, K, H, W, seed=1234 + B * 7 + C + K + H)
     y, ran = run_forward(x, w, pad)
-    expected = 1 if (C % 8 == 0 and K % 16 == 0) else 2
-    assert ran == expected
+    assert ran in expected_paths(C, K)
     check_parity(x, w, pad, y)
+
+
+def fused_eligible(C, K):
+    return 16 <= C <= 64 and C % 16 == 0 and 1 <= K <= 64
+
+
+def expected_paths(C, K):
+    """Paths the automatic dispatch may pick (the fused one only up to a tile count)."""
+    tc = 1 if (C % 8 == 0 and K % 16 == 0) else 2
+    return {tc, 3} if fused_eligible(C, K) else {tc}
+
+
+# Fused single kernel (reference csrc/nova_winograd_fused.hip:283-440, K, C <= 64).
+FUSED_CASES = [
+    (1, 64, 64, 56, 56, 1),      # BASELINE config 1
+    (3, 64, 64, 20, 17, 1),      # ragged tiles, last CTA partly past BP
+    (2, 32, 16, 13, 11, 0),      # pad 0, odd W_out
+    (1, 48, 40, 15, 15, 2),      # C = 48 (three MMA k-steps), K % 16 != 0, pad 2
+    (1, 16, 64, 9, 9, 1),
+    (4, 64, 8, 7, 7, 1),
+    (1, 16, 1, 1, 1, 1),         # single pixel, single output channel
+]
+
+
+@pytest.mark.parametrize("B,C,K,H,W,pad", FUSED_CASES)
+def test_fused_parity(B, C, K, H, W, pad):
+    x, w = o.synthetic_case(B, C, K, H, W, seed=4321 + B + C + K + H + W)
+    y, ran = run_forward(x, w, pad, path=3)
+    assert ran == 3
+    check_parity(x, w, pad, y)
+
+
+def test_fused_matches_three_pass():
+    # Same roundings (V, M to FP16) and the same MMA k-order: only the FP32
+    # order inside the output transform differs.
+    x, w = o.synthetic_case(2, 64, 64, 30, 30, seed=11)
+    y3, r3 = run_forward(x, w, 1, path=3)
+    y1, r1 = run_forward(x, w, 1, path=1)
+    assert (r3, r1) == (3, 1)
+    assert o.rel_l2(y3, y1) < 1e-3
+
+
+def test_fused_refused_outside_its_shapes():
+    L = lib()
+    h = ops.create_handle()
+    try:
+        w = torch.randn(64, 128, 3, 3, device="cuda")
+        ops.check(L.nova_set_weights_v2(h, ops.ptr(w), 64, 128, None), "set_weights")
+        assert L.nova_set_path(h, 3) == 1
+    finally:
+        L.nova_destroy(h)
 
 
 @pytest.mark.parametrize("B,C,K,H,pad", [(1, 64, 64, 28, 1), (2, 128, 64, 14, 1), (1, 64, 96, 9, 0)])
