@@ -262,7 +262,7 @@ int run_forward(Context* ctx, const void* x, void* y, void* V, void* M, int B, i
   const int path = choose_path(ctx, (long long)B * nh * nw);
   if (path == 3) {
     const char* why = "";
-    cudaError_t e = fused_run(ctx->fplan, xh, yh, B, H, W, pad, ctx->d_status, s, &why);
+    cudaError_t e = fused_run(ctx->fplan, xh, yh, B, H, W, pad, ctx->d_status, ctx->num_sms, s, &why);
     if (e != cudaSuccess) return fail(ctx, NOVA_ERR_CUDA, std::string("forward: fused: ") + why);
     ctx->last_path = 3;
     return ok(ctx);

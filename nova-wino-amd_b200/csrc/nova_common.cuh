@@ -77,6 +77,19 @@ __device__ __forceinline__ void bt_1d(const float v[8], float f[8]) {
   f[7] = fmaf(-kB049, v[1], fmaf(kB2211, v[3], fmaf(-kB2721, v[5], v[7])));
 }
 
+// A[i][p] (6 x 8, FP16-rounded entries) as a table, for code that indexes A
+// rather than running the butterfly.
+__host__ __device__ constexpr float kA(int i, int p) {
+  constexpr float a[6][8] = {
+      {1.f, 1.f, 1.f, 1.f, 1.f, 1.f, 1.f, 0.f},
+      {0.f, kA06, -kA06, 1.f, -1.f, kA1167, -kA1167, 0.f},
+      {0.f, kA036, kA036, 1.f, 1.f, kA1361, kA1361, 0.f},
+      {0.f, kA0216, -kA0216, 1.f, -1.f, kA1588, -kA1588, 0.f},
+      {0.f, kA01296, kA01296, 1.f, 1.f, kA1853, kA1853, 0.f},
+      {0.f, kA00778, -kA00778, 1.f, -1.f, kA2161, -kA2161, 1.f}};
+  return a[i][p];
+}
+
 // g[i] = sum_p A[i][p] m[p]  (one 8 -> 6 output-transform pass).
 __device__ __forceinline__ void a_1d(const float m[8], float g[6]) {
   const float sa = m[1] + m[2], da = m[1] - m[2];

@@ -75,6 +75,6 @@ bool fused_supported(int C, int K);
 cudaError_t fused_plan(FusedPlan* plan, const __half* U, int K, int C, const char** why);
 // y = conv(x) for the whole batch; no workspace.
 cudaError_t fused_run(const FusedPlan& plan, const __half* x, __half* y, int B, int H, int W,
-                      int pad, int* dev_status, cudaStream_t s, const char** why);
+                      int pad, int* dev_status, int num_sms, cudaStream_t s, const char** why);
 
 }  // namespace nova

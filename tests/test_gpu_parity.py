@@ -123,6 +123,8 @@ FUSED_CASES = [
     (1, 16, 64, 9, 9, 1),
     (4, 64, 8, 7, 7, 1),
     (1, 16, 1, 1, 1, 1),         # single pixel, single output channel
+    (8, 64, 64, 56, 56, 1),      # 100 groups of 8 tiles: 2-CTA clusters
+    (12, 32, 16, 64, 64, 1),     # 182 groups: one CTA per group
 ]
 
 
