@@ -103,4 +103,61 @@ __device__ __forceinline__ void a_1d(const float m[8], float g[6]) {
   g[5] = fmaf(kA00778, da, fmaf(kA2161, dc, db)) + m[7];
 }
 
+// ---- Programmatic dependent launch ---------------------------------------
+// Hot-path kernels are launched with programmatic stream serialization, so a
+// kernel may start while its predecessor in the stream is still finishing.
+// pdl_wait() blocks until the predecessor grid has completed and its memory
+// is visible; every such kernel calls it before its first global-memory
+// access (read or write).  pdl_trigger() lets the successor start launching
+// once every CTA of this grid has called it (or exited).  Both are no-ops for
+// a normal launch.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+// ---- Paired-lane forms (sm_100 FFMA2 / FADD2 / FMUL2) ----------------------
+// The same butterflies on two independent values at once (two channels).  Each
+// component goes through exactly the operations of bt_1d / a_1d in the same
+// order with the same rounding, so results are bit-identical to the scalar
+// forms; the paired instructions halve the FP32 instruction count.
+__device__ __forceinline__ float2 bc2(float k) { return make_float2(k, k); }
+__device__ __forceinline__ float2 fma2(float k, float2 a, float2 b) {
+  return __ffma2_rn(bc2(k), a, b);
+}
+__device__ __forceinline__ float2 add2(float2 a, float2 b) { return __fadd2_rn(a, b); }
+__device__ __forceinline__ float2 sub2(float2 a, float2 b) {
+  return __fadd2_rn(a, make_float2(-b.x, -b.y));
+}
+__device__ __forceinline__ float2 mul2(float k, float2 a) { return __fmul2_rn(bc2(k), a); }
+
+__device__ __forceinline__ void bt_1d2(const float2 v[8], float2 f[8]) {
+  const float2 e1 = fma2(kB1361, v[2], fma2(-kB2361, v[4], v[6]));
+  const float2 o1 = fma2(kB0817, v[1], fma2(-kB1417, v[3], mul2(kB06, v[5])));
+  const float2 e2 = fma2(kB049, v[2], fma2(-kB1721, v[4], v[6]));
+  const float2 o2 = fma2(kB049, v[1], fma2(-kB1721, v[3], v[5]));
+  const float2 e3 = fma2(kB036, v[2], fma2(-kB1360, v[4], v[6]));
+  const float2 o3 = fma2(kB042, v[1], fma2(-kB1587, v[3], mul2(kB1167, v[5])));
+  f[0] = fma2(-kB049, v[0], fma2(kB2211, v[2], fma2(-kB2721, v[4], v[6])));
+  f[1] = add2(e1, o1);
+  f[2] = sub2(e1, o1);
+  f[3] = add2(e2, o2);
+  f[4] = sub2(e2, o2);
+  f[5] = add2(e3, o3);
+  f[6] = sub2(e3, o3);
+  f[7] = fma2(-kB049, v[1], fma2(kB2211, v[3], fma2(-kB2721, v[5], v[7])));
+}
+
+__device__ __forceinline__ void a_1d2(const float2 m[8], float2 g[6]) {
+  const float2 sa = add2(m[1], m[2]), da = sub2(m[1], m[2]);
+  const float2 sb = add2(m[3], m[4]), db = sub2(m[3], m[4]);
+  const float2 sc = add2(m[5], m[6]), dc = sub2(m[5], m[6]);
+  g[0] = add2(add2(add2(m[0], sa), sb), sc);
+  g[1] = fma2(kA06, da, fma2(kA1167, dc, db));
+  g[2] = fma2(kA036, sa, fma2(kA1361, sc, sb));
+  g[3] = fma2(kA0216, da, fma2(kA1588, dc, db));
+  g[4] = fma2(kA01296, sa, fma2(kA1853, sc, sb));
+  g[5] = add2(fma2(kA00778, da, fma2(kA2161, dc, db)), m[7]);
+}
+
 }  // namespace nova

@@ -213,6 +213,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  pdl_wait();  // x and U come from earlier kernels in the stream
 
   // U prefetch: the ring starts empty, so its first kStages loads need no wait.
   if (threadIdx.x == 0) {
@@ -540,6 +541,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   tc_fence_before();
   __syncthreads();
+  pdl_trigger();  // after the whole CTA is done
   FUSED_MARK(3);
   if (warp == 1) {
     tc_fence_after();
@@ -570,13 +572,15 @@ cudaError_t launch(const CUtensorMap& tmU, const Params& p, long long groups, cu
   cfg.blockDim = dim3(kThreads, 1, 1);
   cfg.dynamicSmemBytes = Cfg<CS>::kSmemBytes;
   cfg.stream = s;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = CS;
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = pdl_enabled(kPdlFused) ? 1 : 0;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = 2;
   cudaError_t e = cudaLaunchKernelEx(&cfg, fused_forward_kernel<CS>, tmU, p);
   if (e != cudaSuccess) *why = "fused kernel launch failed";
   return e;

@@ -114,6 +114,7 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
   const long long tiles_per_pos = (long long)p.n_bp_tiles * p.n_k_tiles;
+  pdl_wait();  // V (and U) come from earlier kernels in the stream
 
   if (warp == 0) {
     if (lane == 0) {
@@ -259,6 +260,7 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
 
   tc_fence_before();
   __syncthreads();
+  pdl_trigger();  // after the whole CTA, epilogue stores included, is done
   if (warp == 1) {
     tc_fence_after();
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base),
@@ -397,8 +399,8 @@ cudaError_t tc_gemm_run(const TcGemmPlan& plan, const __half* V, __half* M, long
   }
   const long long slots = (long long)num_sms * tc::kCtasPerSm;
   long long grid = p.total_tiles < slots ? p.total_tiles : slots;
-  tc::gemm_tc_kernel<<<(unsigned)grid, tc::kThreads, smem, s>>>(tmV, plan.tmU, tmM, p);
-  cudaError_t e = cudaGetLastError();
+  cudaError_t e = launch_pdl(kPdlGemm, tc::gemm_tc_kernel, dim3((unsigned)grid), dim3(tc::kThreads), smem, s,
+                             tmV, plan.tmU, tmM, p);
   if (e != cudaSuccess) *why = "tensor-core GEMM launch failed";
   return e;
 }

@@ -9,7 +9,39 @@
 
 #include "nova_common.cuh"
 
+#include <cstdlib>
+#include <utility>
+
 namespace nova {
+
+// Programmatic dependent launch for the hot-path kernels.  Kinds: 1 = input
+// transform, 2 = tensor-core GEMM, 4 = output transform, 8 = fused kernel;
+// NOVA_PDL_MASK (default: all) selects which kinds launch with it.  The kernel
+// must call pdl_wait() before touching global memory.
+enum PdlKind : int { kPdlInput = 1, kPdlGemm = 2, kPdlOutput = 4, kPdlFused = 8 };
+inline bool pdl_enabled(int kind) {
+  static const int mask = [] {
+    const char* e = std::getenv("NOVA_PDL_MASK");
+    return e ? std::atoi(e) : 15;
+  }();
+  return (mask & kind) != 0;
+}
+
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl(int kind, void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                       cudaStream_t s, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = pdl_enabled(kind) ? 1 : 0;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
 
 // Records code + message as the calling thread's last error (handle-less
 // entry points); returns code.

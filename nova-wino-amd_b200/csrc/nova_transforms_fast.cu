@@ -24,6 +24,23 @@
 namespace nova {
 namespace fast {
 
+#ifdef NOVA_FAST_TRACE
+// Debug builds only: globaltimer stamps per block of the input transform.
+constexpr int kFtBlocks = 16384, kFtSlots = 4;
+__device__ unsigned long long g_fast_trace[kFtBlocks * kFtSlots];
+#define FAST_MARK(i)                                                                  \
+  {                                                                                   \
+    const unsigned _b = blockIdx.x + gridDim.x * blockIdx.y;                          \
+    if (threadIdx.x == 0 && _b < kFtBlocks) {                                         \
+      unsigned long long _t;                                                          \
+      asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(_t));                          \
+      g_fast_trace[_b * kFtSlots + (i)] = _t;                                         \
+    }                                                                                 \
+  }
+#else
+#define FAST_MARK(i)
+#endif
+
 constexpr int kMaxTPC = 6;
 #ifndef NOVA_IT_CHAN_IN_FLIGHT
 #define NOVA_IT_CHAN_IN_FLIGHT 2
@@ -72,7 +89,11 @@ struct Geo {
   // starting at the multiple of 8 at or below w0, landed as [c][r][w].
   static constexpr int kBoxW = ((kInCols + 7 + 7) / 8) * 8;
   static constexpr size_t kLandBytes = (size_t)kCGN * 8 * kBoxW * 2;
-  static constexpr size_t kInSmemTma = 128 + kLandBytes + kInSmem;
+  // TMA path staging [col][channel slot][8 rows]: column pitch kCGN*8 + 8
+  // halves (= 4 mod 32 words, so the transposing stores are conflict-free).
+  static constexpr int kColPitch = kCGN * 8 + 8;
+  static constexpr size_t kInSmemCol = (size_t)kInCols * kColPitch * 2;
+  static constexpr size_t kInSmemTma = 128 + kLandBytes + kInSmemCol;
 };
 
 __device__ __forceinline__ void tma_load_4d(uint32_t dst, const CUtensorMap* map, int c0, int c1,
@@ -116,6 +137,11 @@ __device__ __forceinline__ void block_coords(const Args& a, long long& lrow, int
   th = (int)(grow - (long long)b * a.nh);
 }
 
+// 16-byte slot of channel c inside a staged column: channels rotate within
+// each octet by the octet index, so the 16-byte reads of 8 consecutive lanes
+// (channels 2l or 2l + 1) fall on 8 different bank groups.
+__device__ __forceinline__ int chan_slot(int c) { return (c & ~7) | ((c + (c >> 3)) & 7); }
+
 // kMode: 0 = staged with plain loads; 1 = one TMA tile load of 8 image rows
 // (W % 8 == 0); 2 = one TMA tile load of 5 "pair rows" (2 image rows each, for
 // W % 4 == 0 and even H, where single rows are not 16-byte strided).
@@ -144,6 +170,7 @@ __global__ void __launch_bounds__(32 * Geo<TPC, G>::kWarps, NOVA_IT_MIN_BLOCKS)
   const int h0 = th * 6 - a.pad;
   const int w0 = tw0 * 6 - a.pad;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  pdl_wait();
 
   if constexpr (kMode == 2) {
     // Pair rows: row pr of the landing buffer holds image rows 2(p0+pr) and
@@ -184,6 +211,7 @@ __global__ void __launch_bounds__(32 * Geo<TPC, G>::kWarps, NOVA_IT_MIN_BLOCKS)
     // One TMA tile load brings rows h0..h0+7, columns x0..x0+kBoxW-1 of the
     // block's channels, zero-filled outside the tensor; then lanes (= columns)
     // repack channel pairs into [row][col][channel].
+    FAST_MARK(0);
     const int x0 = w0 >= 0 ? (w0 & ~7) : -((-w0 + 7) & ~7);
     const int d = w0 - x0;
     const uint32_t bar = static_cast<uint32_t>(__cvta_generic_to_shared(&land_bar));
@@ -199,16 +227,33 @@ __global__ void __launch_bounds__(32 * Geo<TPC, G>::kWarps, NOVA_IT_MIN_BLOCKS)
     }
     __syncthreads();
     if (!mbar_wait_bounded(bar, 0)) return;
-    for (int q = warp; q < 8 * (Gm::kCGN / 2); q += Gm::kWarps) {
-      const int r = q & 7, p2 = q >> 3;  // row, channel pair
-      const __half* s0 = land + ((2 * p2) * 8 + r) * Gm::kBoxW + d;
-      const __half* s1 = s0 + 8 * Gm::kBoxW;
-      __half* dst = xs + r * Gm::kInCols * Gm::kPitch + 2 * p2;
-      if (lane < Gm::kInCols)
-        *reinterpret_cast<__half2*>(dst + lane * Gm::kPitch) = __halves2half2(s0[lane], s1[lane]);
-      if (lane + 32 < Gm::kInCols)
-        *reinterpret_cast<__half2*>(dst + (lane + 32) * Gm::kPitch) =
-            __halves2half2(s0[lane + 32], s1[lane + 32]);
+    FAST_MARK(1);
+    // Transpose [channel][row][col] into [col][channel slot][row] with
+    // ldmatrix.trans: one 8x8 matrix = (channel, rows 0-7, 8 columns); lane T
+    // gets rows 2(T%4), 2(T%4)+1 of column T/4, i.e. one 32-bit word of the
+    // destination.
+    constexpr int kChunks = Gm::kBoxW / 8;
+    constexpr int kQuads = Gm::kCGN / 4;
+    const uint32_t land_s = static_cast<uint32_t>(__cvta_generic_to_shared(land));
+    const uint32_t xs_s = static_cast<uint32_t>(__cvta_generic_to_shared(xs));
+    for (int m4 = warp; m4 < kQuads * kChunks; m4 += Gm::kWarps) {
+      const int cq = m4 % kQuads, chunk = m4 / kQuads;
+      const uint32_t src = land_s + (uint32_t)((((cq * 4 + (lane >> 3)) * 8 + (lane & 7)) *
+                                                    Gm::kBoxW + chunk * 8) * 2);
+      uint32_t rg[4];
+      asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0, %1, %2, %3}, [%4];"
+                   : "=r"(rg[0]), "=r"(rg[1]), "=r"(rg[2]), "=r"(rg[3])
+                   : "r"(src)
+                   : "memory");
+      const int col = chunk * 8 + (lane >> 2) - d;
+      if (col >= 0 && col < Gm::kInCols) {
+        const uint32_t dst = xs_s + (uint32_t)((col * Gm::kColPitch + 2 * (lane & 3)) * 2);
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+          asm volatile("st.shared.b32 [%0], %1;" ::"r"(dst + (uint32_t)chan_slot(cq * 4 + i) * 16u),
+                       "r"(rg[i])
+                       : "memory");
+      }
     }
   } else {
   // Stage rows h0..h0+7 of the block's channels, columns w0..w0+kInCols-1.
@@ -260,6 +305,7 @@ __global__ void __launch_bounds__(32 * Geo<TPC, G>::kWarps, NOVA_IT_MIN_BLOCKS)
   }
   }
   __syncthreads();
+  if (kMode == 1) FAST_MARK(2);
 
   const long long plane = a.BP * (long long)C;
   for (int it = warp; it < TPC * G; it += Gm::kWarps) {
@@ -267,39 +313,49 @@ __global__ void __launch_bounds__(32 * Geo<TPC, G>::kWarps, NOVA_IT_MIN_BLOCKS)
     if (t >= ntw) break;
     const int cl = g * 64 + 2 * lane;
     const int c = c0 + cl;
-    float ta[8][8], tb[8][8];
+    float2 tt[8][8];  // the lane's channel pair, paired in every operation
 #pragma unroll
     for (int j = 0; j < 8; ++j) {  // columns: tmp[.][j] = B^T d[.][j]
-      float va[8], vb[8], fa[8], fb[8];
+      float2 v[8], f[8];
+      if constexpr (kMode == 1) {
+        const __half* colp = xs + (t * 6 + j) * Gm::kColPitch;
+        const uint4 wa = *reinterpret_cast<const uint4*>(colp + chan_slot(cl) * 8);
+        const uint4 wb = *reinterpret_cast<const uint4*>(colp + chan_slot(cl + 1) * 8);
+        const uint32_t ua[4] = {wa.x, wa.y, wa.z, wa.w}, ub[4] = {wb.x, wb.y, wb.z, wb.w};
 #pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        const __half2 p = *reinterpret_cast<const __half2*>(
-            xs + (i * Gm::kInCols + t * 6 + j) * Gm::kPitch + cl);
-        const float2 f = __half22float2(p);
-        va[i] = f.x;
-        vb[i] = f.y;
-      }
-      bt_1d(va, fa);
-      bt_1d(vb, fb);
+        for (int i2 = 0; i2 < 4; ++i2) {
+          const float2 fa = __half22float2(*reinterpret_cast<const __half2*>(&ua[i2]));
+          const float2 fb = __half22float2(*reinterpret_cast<const __half2*>(&ub[i2]));
+          v[2 * i2] = make_float2(fa.x, fb.x);
+          v[2 * i2 + 1] = make_float2(fa.y, fb.y);
+        }
+      } else {
 #pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        ta[i][j] = fa[i];
-        tb[i][j] = fb[i];
+        for (int i = 0; i < 8; ++i)
+          v[i] = __half22float2(*reinterpret_cast<const __half2*>(
+              xs + (i * Gm::kInCols + t * 6 + j) * Gm::kPitch + cl));
       }
+      bt_1d2(v, f);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) tt[i][j] = f[i];
     }
     if (c < C) {  // C is even: the pair is wholly in or out
       __half2* out = reinterpret_cast<__half2*>(V + (lrow * a.nw + tw0 + t) * C + c);
 #pragma unroll
       for (int r = 0; r < 8; ++r) {  // rows: V[r][.] = tmp[r][.] B
-        float fa[8], fb[8];
-        bt_1d(ta[r], fa);
-        bt_1d(tb[r], fb);
+        float2 f[8];
+        bt_1d2(tt[r], f);
 #pragma unroll
-        for (int s = 0; s < 8; ++s)
-          out[(long long)(r * 8 + s) * (plane >> 1)] = __floats2half2_rn(fa[s], fb[s]);
+        for (int s = 0; s < 8; ++s) out[(long long)(r * 8 + s) * (plane >> 1)] = __float22half2_rn(f[s]);
       }
     }
   }
+  __syncthreads();
+  pdl_trigger();  // after the whole block is done
+#ifdef NOVA_FAST_TRACE
+  __syncthreads();
+  if (kMode == 1) FAST_MARK(3);
+#endif
 }
 
 template <int TPC, int G>
@@ -315,6 +371,7 @@ __global__ void __launch_bounds__(32 * Geo<TPC, G>::kWarps, NOVA_OT_MIN_BLOCKS)
   const int tw0 = twc * TPC;
   const int ntw = min(TPC, a.nw - tw0);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  pdl_wait();
   const long long plane = a.BP * (long long)K;
 
   for (int it = warp; it < TPC * G; it += Gm::kWarps) {
@@ -325,34 +382,26 @@ __global__ void __launch_bounds__(32 * Geo<TPC, G>::kWarps, NOVA_OT_MIN_BLOCKS)
     const bool kok = k < K;
     const __half2* in =
         reinterpret_cast<const __half2*>(M + (lrow * a.nw + tw0 + t) * K + (kok ? k : 0));
-    float ta[6][8], tb[6][8];
+    float2 tt[6][8];  // the lane's channel pair, paired in every operation
 #pragma unroll
     for (int q = 0; q < 8; ++q) {  // columns: tmp[.][q] = A m[.][q]
-      float ma[8], mb[8], ga[6], gb[6];
+      float2 m[8], g[6];
 #pragma unroll
-      for (int p = 0; p < 8; ++p) {
-        const float2 f = kok ? __half22float2(in[(long long)(p * 8 + q) * (plane >> 1)])
-                             : make_float2(0.f, 0.f);
-        ma[p] = f.x;
-        mb[p] = f.y;
-      }
-      a_1d(ma, ga);
-      a_1d(mb, gb);
+      for (int p = 0; p < 8; ++p)
+        m[p] = kok ? __half22float2(in[(long long)(p * 8 + q) * (plane >> 1)])
+                   : make_float2(0.f, 0.f);
+      a_1d2(m, g);
 #pragma unroll
-      for (int i = 0; i < 6; ++i) {
-        ta[i][q] = ga[i];
-        tb[i][q] = gb[i];
-      }
+      for (int i = 0; i < 6; ++i) tt[i][q] = g[i];
     }
 #pragma unroll
     for (int i = 0; i < 6; ++i) {  // rows: Y[i][.] = tmp[i][.] A^T
-      float ga[6], gb[6];
-      a_1d(ta[i], ga);
-      a_1d(tb[i], gb);
+      float2 g[6];
+      a_1d2(tt[i], g);
 #pragma unroll
       for (int j = 0; j < 6; ++j)
         *reinterpret_cast<__half2*>(ys + (i * Gm::kOutCols + t * 6 + j) * Gm::kPitch + kl) =
-            __floats2half2_rn(ga[j], gb[j]);
+            __float22half2_rn(g[j]);
     }
   }
   __syncthreads();
@@ -375,6 +424,8 @@ __global__ void __launch_bounds__(32 * Geo<TPC, G>::kWarps, NOVA_OT_MIN_BLOCKS)
       }
     }
   }
+  __syncthreads();
+  pdl_trigger();  // after the whole block is done
 }
 
 // ---------------------------------------------------------------------------
@@ -384,7 +435,9 @@ __global__ void __launch_bounds__(32 * Geo<TPC, G>::kWarps, NOVA_OT_MIN_BLOCKS)
 // lane's plane elements and their shared-memory cells are computed once per
 // block), and the output is written back as whole contiguous planes.
 // ---------------------------------------------------------------------------
-template <int TR, int TC>
+// kW > 0 fixes the warps per block (small batches: one warp per tile, so a
+// block finishes its image in one round); kW = 0 is the throughput shape.
+template <int TR, int TC, int kW = 0>
 struct PlaneGeo {
   static constexpr int kRows = TR * 6 + 2, kCols = TC * 6 + 2;    // padded input
   static constexpr int kCells = kRows * kCols;
@@ -396,7 +449,8 @@ struct PlaneGeo {
 #define NOVA_PLANE_MAX_WARPS 5  // measured: 3x3-tile images run best at 5 warps, 3 blocks/SM
 #endif
   static constexpr int kWarps =
-      TR * TC < 2 ? 2 : (TR * TC > NOVA_PLANE_MAX_WARPS ? NOVA_PLANE_MAX_WARPS : TR * TC);
+      kW > 0 ? kW
+             : (TR * TC < 2 ? 2 : (TR * TC > NOVA_PLANE_MAX_WARPS ? NOVA_PLANE_MAX_WARPS : TR * TC));
   // Blocks per SM the register budget is sized for (about 128 registers/thread).
   static constexpr int kMinBlocks = 65536 / (128 * 32 * kWarps) < 1 ? 1 : 65536 / (128 * 32 * kWarps);
   static constexpr size_t kInSmem = (size_t)kCells * kPitch * 2;
@@ -405,10 +459,10 @@ struct PlaneGeo {
 
 // Plane args: BP/row window semantics as Args; row0 and lrow0 are tile rows and
 // are multiples of nh here (blocks own whole images).
-template <int TR, int TC>
-__global__ void __launch_bounds__(32 * PlaneGeo<TR, TC>::kWarps, PlaneGeo<TR, TC>::kMinBlocks)
+template <int TR, int TC, int kW>
+__global__ void __launch_bounds__(32 * PlaneGeo<TR, TC, kW>::kWarps, PlaneGeo<TR, TC, kW>::kMinBlocks)
     input_transform_plane(const __half* __restrict__ x, __half* __restrict__ V, const Args a) {
-  using Pg = PlaneGeo<TR, TC>;
+  using Pg = PlaneGeo<TR, TC, kW>;
   extern __shared__ __align__(16) __half xs[];  // [kCells][kPitch]
   const int cg = blockIdx.x;
   const long long limg = a.lrow0 / TR + blockIdx.y;  // image inside the window
@@ -416,6 +470,7 @@ __global__ void __launch_bounds__(32 * PlaneGeo<TR, TC>::kWarps, PlaneGeo<TR, TC
   const int C = a.C, H = a.H, W = a.W, pad = a.pad;
   const int c0 = cg * 64;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  pdl_wait();
 
   // Lane's padded-plane cells: global offset inside the image plane (or -1 for
   // zero padding) and shared-memory cell offset.
@@ -448,45 +503,38 @@ __global__ void __launch_bounds__(32 * PlaneGeo<TR, TC>::kWarps, PlaneGeo<TR, TC
     const int tr = t / TC, tc = t - (t / TC) * TC;
     const int cl = 2 * lane;
     const int c = c0 + cl;
-    float ta[8][8], tb[8][8];
+    float2 tt[8][8];
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
-      float va[8], vb[8], fa[8], fb[8];
+      float2 v[8], f[8];
 #pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        const float2 f = __half22float2(*reinterpret_cast<const __half2*>(
+      for (int i = 0; i < 8; ++i)
+        v[i] = __half22float2(*reinterpret_cast<const __half2*>(
             xs + ((tr * 6 + i) * Pg::kCols + tc * 6 + j) * Pg::kPitch + cl));
-        va[i] = f.x;
-        vb[i] = f.y;
-      }
-      bt_1d(va, fa);
-      bt_1d(vb, fb);
+      bt_1d2(v, f);
 #pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        ta[i][j] = fa[i];
-        tb[i][j] = fb[i];
-      }
+      for (int i = 0; i < 8; ++i) tt[i][j] = f[i];
     }
     if (c < C) {
       const long long bp = (limg * TR + tr) * TC + tc;
       __half2* out = reinterpret_cast<__half2*>(V + bp * C + c);
 #pragma unroll
       for (int r = 0; r < 8; ++r) {
-        float fa[8], fb[8];
-        bt_1d(ta[r], fa);
-        bt_1d(tb[r], fb);
+        float2 f[8];
+        bt_1d2(tt[r], f);
 #pragma unroll
-        for (int s = 0; s < 8; ++s)
-          out[(long long)(r * 8 + s) * (plane >> 1)] = __floats2half2_rn(fa[s], fb[s]);
+        for (int s = 0; s < 8; ++s) out[(long long)(r * 8 + s) * (plane >> 1)] = __float22half2_rn(f[s]);
       }
     }
   }
+  __syncthreads();
+  pdl_trigger();  // after the whole block is done
 }
 
-template <int TR, int TC>
-__global__ void __launch_bounds__(32 * PlaneGeo<TR, TC>::kWarps, PlaneGeo<TR, TC>::kMinBlocks)
+template <int TR, int TC, int kW>
+__global__ void __launch_bounds__(32 * PlaneGeo<TR, TC, kW>::kWarps, PlaneGeo<TR, TC, kW>::kMinBlocks)
     output_transform_plane(const __half* __restrict__ M, __half* __restrict__ y, const Args a) {
-  using Pg = PlaneGeo<TR, TC>;
+  using Pg = PlaneGeo<TR, TC, kW>;
   extern __shared__ __align__(16) __half ys[];  // [kOutCells][kPitch]
   const int kg = blockIdx.x;
   const long long limg = a.lrow0 / TR + blockIdx.y;
@@ -494,6 +542,7 @@ __global__ void __launch_bounds__(32 * PlaneGeo<TR, TC>::kWarps, PlaneGeo<TR, TC
   const int K = a.C, H_out = a.H, W_out = a.W;
   const int k0 = kg * 64;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  pdl_wait();
   const long long plane = a.BP * (long long)K;
 
   for (int t = warp; t < TR * TC; t += Pg::kWarps) {
@@ -503,34 +552,26 @@ __global__ void __launch_bounds__(32 * PlaneGeo<TR, TC>::kWarps, PlaneGeo<TR, TC
     const bool kok = k < K;
     const long long bp = (limg * TR + tr) * TC + tc;
     const __half2* in = reinterpret_cast<const __half2*>(M + bp * K + (kok ? k : 0));
-    float ta[6][8], tb[6][8];
+    float2 tt[6][8];
 #pragma unroll
     for (int q = 0; q < 8; ++q) {
-      float ma[8], mb[8], ga[6], gb[6];
+      float2 m[8], g[6];
 #pragma unroll
-      for (int p = 0; p < 8; ++p) {
-        const float2 f = kok ? __half22float2(in[(long long)(p * 8 + q) * (plane >> 1)])
-                             : make_float2(0.f, 0.f);
-        ma[p] = f.x;
-        mb[p] = f.y;
-      }
-      a_1d(ma, ga);
-      a_1d(mb, gb);
+      for (int p = 0; p < 8; ++p)
+        m[p] = kok ? __half22float2(in[(long long)(p * 8 + q) * (plane >> 1)])
+                   : make_float2(0.f, 0.f);
+      a_1d2(m, g);
 #pragma unroll
-      for (int i = 0; i < 6; ++i) {
-        ta[i][q] = ga[i];
-        tb[i][q] = gb[i];
-      }
+      for (int i = 0; i < 6; ++i) tt[i][q] = g[i];
     }
 #pragma unroll
     for (int i = 0; i < 6; ++i) {
-      float ga[6], gb[6];
-      a_1d(ta[i], ga);
-      a_1d(tb[i], gb);
+      float2 g[6];
+      a_1d2(tt[i], g);
 #pragma unroll
       for (int j = 0; j < 6; ++j)
         *reinterpret_cast<__half2*>(ys + ((tr * 6 + i) * (TC * 6) + tc * 6 + j) * Pg::kPitch +
-                                    kl) = __floats2half2_rn(ga[j], gb[j]);
+                                    kl) = __float22half2_rn(g[j]);
     }
   }
   __syncthreads();
@@ -552,36 +593,70 @@ __global__ void __launch_bounds__(32 * PlaneGeo<TR, TC>::kWarps, PlaneGeo<TR, TC
     for (int m = 0; m < Pg::kOutPerLane; ++m)
       if (soff[m] >= 0) dst[lane + 32 * m] = ys[soff[m] + kl];
   }
+  __syncthreads();
+  pdl_trigger();  // after the whole block is done
 }
 
 // Kernel addresses for the shared-memory opt-in.
-template <int TR, int TC>
-const void* it_plane_fn() { return (const void*)input_transform_plane<TR, TC>; }
-template <int TR, int TC>
-const void* ot_plane_fn() { return (const void*)output_transform_plane<TR, TC>; }
+template <int TR, int TC, int kW>
+const void* it_plane_fn() { return (const void*)input_transform_plane<TR, TC, kW>; }
+template <int TR, int TC, int kW>
+const void* ot_plane_fn() { return (const void*)output_transform_plane<TR, TC, kW>; }
+
+// Blocks of the plane kernels a launch needs before the throughput shape
+// (5 warps, several blocks per SM) beats one warp per tile.
+static bool plane_small(long long blocks) {
+  static int sms[64] = {};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return false;
+  if (!sms[dev]) cudaDeviceGetAttribute(&sms[dev], cudaDevAttrMultiProcessorCount, dev);
+  return blocks < sms[dev];
+}
+
+template <int TR, int TC, int kW>
+static void launch_it_plane_w(const __half* x, __half* V, Args a, long long nimg, unsigned gx,
+                              cudaStream_t s) {
+  using Pg = PlaneGeo<TR, TC, kW>;
+  if (!smem_optin_once<it_plane_fn<TR, TC, kW>>(Pg::kInSmem)) return;
+  for (long long done = 0; done < nimg; done += kMaxGridY) {
+    a.lrow0 = done * TR;
+    dim3 grid(gx, (unsigned)std::min(kMaxGridY, nimg - done));
+    launch_pdl(kPdlInput, input_transform_plane<TR, TC, kW>, grid, dim3(32 * Pg::kWarps),
+               Pg::kInSmem, s, x, V, a);
+  }
+}
 
 template <int TR, int TC>
 static void launch_it_plane(const __half* x, __half* V, Args a, long long nimg, unsigned gx,
                             cudaStream_t s) {
-  using Pg = PlaneGeo<TR, TC>;
-  if (!smem_optin_once<it_plane_fn<TR, TC>>(Pg::kInSmem)) return;
+  constexpr int kOne = TR * TC < 2 ? 2 : TR * TC;
+  if (TR * TC > NOVA_PLANE_MAX_WARPS && plane_small(nimg * gx))
+    launch_it_plane_w<TR, TC, kOne>(x, V, a, nimg, gx, s);
+  else
+    launch_it_plane_w<TR, TC, 0>(x, V, a, nimg, gx, s);
+}
+
+template <int TR, int TC, int kW>
+static void launch_ot_plane_w(const __half* M, __half* y, Args a, long long nimg, unsigned gx,
+                              cudaStream_t s) {
+  using Pg = PlaneGeo<TR, TC, kW>;
+  if (!smem_optin_once<ot_plane_fn<TR, TC, kW>>(Pg::kOutSmem)) return;
   for (long long done = 0; done < nimg; done += kMaxGridY) {
     a.lrow0 = done * TR;
     dim3 grid(gx, (unsigned)std::min(kMaxGridY, nimg - done));
-    input_transform_plane<TR, TC><<<grid, 32 * Pg::kWarps, Pg::kInSmem, s>>>(x, V, a);
+    launch_pdl(kPdlOutput, output_transform_plane<TR, TC, kW>, grid, dim3(32 * Pg::kWarps),
+               Pg::kOutSmem, s, M, y, a);
   }
 }
 
 template <int TR, int TC>
 static void launch_ot_plane(const __half* M, __half* y, Args a, long long nimg, unsigned gx,
                             cudaStream_t s) {
-  using Pg = PlaneGeo<TR, TC>;
-  if (!smem_optin_once<ot_plane_fn<TR, TC>>(Pg::kOutSmem)) return;
-  for (long long done = 0; done < nimg; done += kMaxGridY) {
-    a.lrow0 = done * TR;
-    dim3 grid(gx, (unsigned)std::min(kMaxGridY, nimg - done));
-    output_transform_plane<TR, TC><<<grid, 32 * Pg::kWarps, Pg::kOutSmem, s>>>(M, y, a);
-  }
+  constexpr int kOne = TR * TC < 2 ? 2 : TR * TC;
+  if (TR * TC > NOVA_PLANE_MAX_WARPS && plane_small(nimg * gx))
+    launch_ot_plane_w<TR, TC, kOne>(M, y, a, nimg, gx, s);
+  else
+    launch_ot_plane_w<TR, TC, 0>(M, y, a, nimg, gx, s);
 }
 
 #define NOVA_PLANE_SWITCH(TR_VAL, TC_VAL, FN, ...)  \
@@ -700,11 +775,11 @@ static void launch_it(const __half* x, __half* V, Args a, long long nrows, unsig
     dim3 grid(gx, (unsigned)std::min(kMaxGridY, nrows - done));
     const unsigned thr = 32 * Gm::kWarps;
     if (mode == 1)
-      input_transform_fast<TPC, G, 1><<<grid, thr, smem, s>>>(x, V, map, a);
+      launch_pdl(kPdlInput, input_transform_fast<TPC, G, 1>, grid, dim3(thr), smem, s, x, V, map, a);
     else if (mode == 2)
-      input_transform_fast<TPC, G, 2><<<grid, thr, smem, s>>>(x, V, map, a);
+      launch_pdl(kPdlInput, input_transform_fast<TPC, G, 2>, grid, dim3(thr), smem, s, x, V, map, a);
     else
-      input_transform_fast<TPC, G, 0><<<grid, thr, smem, s>>>(x, V, map, a);
+      launch_pdl(kPdlInput, input_transform_fast<TPC, G, 0>, grid, dim3(thr), smem, s, x, V, map, a);
   }
 }
 
@@ -714,7 +789,7 @@ static void launch_ot(const __half* M, __half* y, Args a, long long nrows, unsig
   for (long long done = 0; done < nrows; done += kMaxGridY) {
     a.lrow0 = done;
     dim3 grid(gx, (unsigned)std::min(kMaxGridY, nrows - done));
-    output_transform_fast<TPC, G><<<grid, 32 * Geo<TPC, G>::kWarps, 0, s>>>(M, y, a);
+    launch_pdl(kPdlOutput, output_transform_fast<TPC, G>, grid, dim3(32 * Geo<TPC, G>::kWarps), 0, s, M, y, a);
   }
 }
 
@@ -731,6 +806,15 @@ static void launch_ot(const __half* M, __half* y, Args a, long long nrows, unsig
   }
 
 }  // namespace fast
+
+#ifdef NOVA_FAST_TRACE
+extern "C" __attribute__((visibility("default"))) int nova_debug_fast_trace(
+    unsigned long long* out, int n_blocks) {
+  if (n_blocks > fast::kFtBlocks) n_blocks = fast::kFtBlocks;
+  return (int)cudaMemcpyFromSymbol(out, fast::g_fast_trace,
+                                   sizeof(unsigned long long) * fast::kFtSlots * (size_t)n_blocks);
+}
+#endif
 
 cudaError_t launch_input_transform_fast(const __half* x, __half* V, int B, int C, int H, int W,
                                         int pad, int nh, int nw, long long row0, long long nrows,
