@@ -7,12 +7,15 @@
 // every access a warp makes to one position of V or M is one aligned half2 per
 // lane = one full 128-byte line.
 //
-// Input transform:  image rows staged in shared memory [row][col][channel]
-//   (66-half cell pitch = 33 words, odd: conflict-free both for the row-wise
-//   staging stores and for the lane-pair reads), then V = B^T d B in
-//   registers, written straight to V[pos][bp][c].
-// Output transform: M read straight from M[pos][bp][k] (64 independent loads per
-//   lane), Y = A M A^T in registers, parked in shared memory [row][col][k], then
+// Input transform:  image rows staged in shared memory, then V = B^T d B in
+//   registers.  With W % 8 == 0 (mode 1) the rows arrive by one TMA tile load,
+//   are transposed with ldmatrix.trans into [col][channel][row], and the V
+//   tiles go back out through shared memory by TMA tile stores; otherwise the
+//   staging is [row][col][channel] (66-half cell pitch = 33 words, odd:
+//   conflict-free) and V is written straight to V[pos][bp][c].
+// Output transform: the block's M tiles arrive by TMA tile loads (or 64
+//   independent loads per lane when M cannot be described by a tensor map),
+//   Y = A M A^T in registers, parked in shared memory [row][col][k], then
 //   written as whole output row segments along w (warp per row, lane per
 //   column).
 // Reference: input_transform_kernel(_mt) and output_transform_kernel(_mt),
@@ -20,6 +23,7 @@
 #include <algorithm>
 
 #include "nova_internal.h"
+#include "nova_tc_ptx.cuh"
 
 namespace nova {
 namespace fast {
@@ -54,10 +58,12 @@ constexpr int kMaxTPC = 6;
 constexpr long long kMaxGridY = 65535;
 
 // Dynamic shared memory above 48 KB is a per-device, per-kernel opt-in.
+// static_bytes: the kernel's static shared memory; the opt-in is needed once
+// static + dynamic exceeds 48 KB.
 template <const void* (*Fn)()>
-static bool smem_optin_once(size_t bytes) {
+static bool smem_optin_once(size_t bytes, size_t static_bytes = 0) {
   static bool done[64] = {};
-  if (bytes <= 48 * 1024) return true;
+  if (bytes + static_bytes <= 48 * 1024) return true;
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return false;
   if (done[dev]) return true;
@@ -148,7 +154,8 @@ __device__ __forceinline__ int chan_slot(int c) { return (c & ~7) | ((c + (c >> 
 template <int TPC, int G, int kMode>
 __global__ void __launch_bounds__(32 * Geo<TPC, G>::kWarps, NOVA_IT_MIN_BLOCKS)
     input_transform_fast(const __half* __restrict__ x, __half* __restrict__ V,
-                         const __grid_constant__ CUtensorMap map_x, const Args a) {
+                         const __grid_constant__ CUtensorMap map_x,
+                         const __grid_constant__ CUtensorMap map_v, const Args a) {
   using Gm = Geo<TPC, G>;
   extern __shared__ uint8_t it_raw[];
   uint8_t* it_base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(it_raw) + 127) &
@@ -159,6 +166,7 @@ __global__ void __launch_bounds__(32 * Geo<TPC, G>::kWarps, NOVA_IT_MIN_BLOCKS)
       kMode == 1 ? Gm::kLandBytes
                  : (kMode == 2 ? (((size_t)Gm::kCGN * 5 * 2 * a.W * 2 + 127) / 128) * 128 : 0);
   __half* xs = reinterpret_cast<__half*>(it_base + land_bytes);
+  const uint32_t land_s = static_cast<uint32_t>(__cvta_generic_to_shared(land));
   __shared__ uint64_t land_bar;
   long long lrow;
   int b, th, twc, cg;
@@ -209,8 +217,8 @@ __global__ void __launch_bounds__(32 * Geo<TPC, G>::kWarps, NOVA_IT_MIN_BLOCKS)
     }
   } else if constexpr (kMode == 1) {
     // One TMA tile load brings rows h0..h0+7, columns x0..x0+kBoxW-1 of the
-    // block's channels, zero-filled outside the tensor; then lanes (= columns)
-    // repack channel pairs into [row][col][channel].
+    // block's channels, zero-filled outside the tensor, as [channel][row][col];
+    // ldmatrix.trans then turns it into [col][channel slot][row].
     FAST_MARK(0);
     const int x0 = w0 >= 0 ? (w0 & ~7) : -((-w0 + 7) & ~7);
     const int d = w0 - x0;
@@ -234,7 +242,6 @@ __global__ void __launch_bounds__(32 * Geo<TPC, G>::kWarps, NOVA_IT_MIN_BLOCKS)
     // destination.
     constexpr int kChunks = Gm::kBoxW / 8;
     constexpr int kQuads = Gm::kCGN / 4;
-    const uint32_t land_s = static_cast<uint32_t>(__cvta_generic_to_shared(land));
     const uint32_t xs_s = static_cast<uint32_t>(__cvta_generic_to_shared(xs));
     for (int m4 = warp; m4 < kQuads * kChunks; m4 += Gm::kWarps) {
       const int cq = m4 % kQuads, chunk = m4 / kQuads;
@@ -339,7 +346,25 @@ __global__ void __launch_bounds__(32 * Geo<TPC, G>::kWarps, NOVA_IT_MIN_BLOCKS)
 #pragma unroll
       for (int i = 0; i < 8; ++i) tt[i][j] = f[i];
     }
-    if (c < C) {  // C is even: the pair is wholly in or out
+    if constexpr (kMode == 1) {
+      // V tile [pos][kCGN] into the landing buffer, which the repack has freed;
+      // channels past C are clipped by the TMA store.
+      const uint32_t vrow = land_s + (uint32_t)((t * 64 * Gm::kCGN + cl) * 2);
+#pragma unroll
+      for (int r = 0; r < 8; ++r) {  // rows: V[r][.] = tmp[r][.] B
+        float2 f[8];
+        bt_1d2(tt[r], f);
+#pragma unroll
+        for (int s = 0; s < 8; ++s) {
+          const __half2 hv = __float22half2_rn(f[s]);
+          asm volatile("st.shared.b32 [%0], %1;" ::"r"(vrow + (uint32_t)((r * 8 + s) *
+                                                                         Gm::kCGN * 2)),
+                       "r"(*reinterpret_cast<const uint32_t*>(&hv))
+                       : "memory");
+        }
+      }
+    } else {
+      if (c >= C) continue;  // C is even: the pair is wholly in or out
       __half2* out = reinterpret_cast<__half2*>(V + (lrow * a.nw + tw0 + t) * C + c);
 #pragma unroll
       for (int r = 0; r < 8; ++r) {  // rows: V[r][.] = tmp[r][.] B
@@ -350,6 +375,17 @@ __global__ void __launch_bounds__(32 * Geo<TPC, G>::kWarps, NOVA_IT_MIN_BLOCKS)
       }
     }
   }
+  if constexpr (kMode == 1) {
+    tc::fence_async_smem();  // the staged V tiles are visible to the TMA unit
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      for (int t = 0; t < ntw; ++t)
+        tc::tma_store_3d(&map_v, land_s + (uint32_t)(t * 64 * Gm::kCGN * 2), c0,
+                         (int)(lrow * a.nw + tw0 + t), 0);
+      tc::bulk_commit();
+      tc::bulk_wait_read_all();  // shared memory stays valid until the stores read it
+    }
+  }
   __syncthreads();
   pdl_trigger();  // after the whole block is done
 #ifdef NOVA_FAST_TRACE
@@ -358,11 +394,16 @@ __global__ void __launch_bounds__(32 * Geo<TPC, G>::kWarps, NOVA_IT_MIN_BLOCKS)
 #endif
 }
 
-template <int TPC, int G>
+// kTmaIn: the block's M tiles ([pos][channels] each) arrive by TMA tile loads
+// into shared memory instead of 64 scattered 4-byte loads per lane.
+template <int TPC, int G, bool kTmaIn>
 __global__ void __launch_bounds__(32 * Geo<TPC, G>::kWarps, NOVA_OT_MIN_BLOCKS)
-    output_transform_fast(const __half* __restrict__ M, __half* __restrict__ y, const Args a) {
+    output_transform_fast(const __half* __restrict__ M, __half* __restrict__ y,
+                          const __grid_constant__ CUtensorMap map_m, const Args a) {
   using Gm = Geo<TPC, G>;
   __shared__ __align__(16) __half ys[6 * Gm::kOutCols * Gm::kPitch];
+  extern __shared__ uint8_t ot_raw[];
+  __shared__ uint64_t m_bar;
   long long lrow;
   int b, th, twc, kg;
   block_coords(a, lrow, b, th, twc, kg);
@@ -373,6 +414,22 @@ __global__ void __launch_bounds__(32 * Geo<TPC, G>::kWarps, NOVA_OT_MIN_BLOCKS)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   pdl_wait();
   const long long plane = a.BP * (long long)K;
+  const __half* mtiles = reinterpret_cast<const __half*>(
+      (reinterpret_cast<uintptr_t>(ot_raw) + 127) & ~uintptr_t(127));
+  if constexpr (kTmaIn) {
+    const uint32_t bar = static_cast<uint32_t>(__cvta_generic_to_shared(&m_bar));
+    if (threadIdx.x == 0) {
+      const uint32_t dst = static_cast<uint32_t>(__cvta_generic_to_shared(mtiles));
+      asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(bar) : "memory");
+      asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+      tc::mbar_expect_tx(bar, (uint32_t)(ntw * 64 * Gm::kCGN * 2));
+      for (int t = 0; t < ntw; ++t)
+        tc::tma_load_3d(dst + (uint32_t)(t * 64 * Gm::kCGN * 2), &map_m, k0,
+                        (int)(lrow * a.nw + tw0 + t), 0, bar);
+    }
+    __syncthreads();
+    if (!mbar_wait_bounded(bar, 0)) return;
+  }
 
   for (int it = warp; it < TPC * G; it += Gm::kWarps) {
     const int t = it / G, g = it % G;
@@ -382,14 +439,19 @@ __global__ void __launch_bounds__(32 * Geo<TPC, G>::kWarps, NOVA_OT_MIN_BLOCKS)
     const bool kok = k < K;
     const __half2* in =
         reinterpret_cast<const __half2*>(M + (lrow * a.nw + tw0 + t) * K + (kok ? k : 0));
+    const __half* mt = mtiles + t * 64 * Gm::kCGN + kl;
     float2 tt[6][8];  // the lane's channel pair, paired in every operation
 #pragma unroll
     for (int q = 0; q < 8; ++q) {  // columns: tmp[.][q] = A m[.][q]
       float2 m[8], g[6];
 #pragma unroll
-      for (int p = 0; p < 8; ++p)
-        m[p] = kok ? __half22float2(in[(long long)(p * 8 + q) * (plane >> 1)])
-                   : make_float2(0.f, 0.f);
+      for (int p = 0; p < 8; ++p) {
+        if constexpr (kTmaIn)
+          m[p] = __half22float2(*reinterpret_cast<const __half2*>(mt + (p * 8 + q) * Gm::kCGN));
+        else
+          m[p] = kok ? __half22float2(in[(long long)(p * 8 + q) * (plane >> 1)])
+                     : make_float2(0.f, 0.f);
+      }
       a_1d2(m, g);
 #pragma unroll
       for (int i = 0; i < 6; ++i) tt[i][q] = g[i];
@@ -749,16 +811,33 @@ static bool encode_x_pair_map(CUtensorMap* map, const __half* x, int B, int C, i
             CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+// V as [64 pos][BP][C] (C fastest), box {cgn, 1 tile, 64 pos}: one TMA store
+// per staged tile.  Needs C % 8 == 0 (16-byte strides) and BP < 2^31.
+static bool encode_v_map(CUtensorMap* map, const __half* V, int C, long long BP, int cgn) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn || (C % 8) || BP <= 0 || BP >= (1ll << 31) ||
+      (reinterpret_cast<uintptr_t>(V) & 15))
+    return false;
+  cuuint64_t dims[3] = {(cuuint64_t)C, (cuuint64_t)BP, 64};
+  cuuint64_t strides[2] = {(cuuint64_t)C * 2, (cuuint64_t)C * 2 * (cuuint64_t)BP};
+  cuuint32_t box[3] = {(cuuint32_t)cgn, 1, 64};
+  cuuint32_t estr[3] = {1, 1, 1};
+  return fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, const_cast<__half*>(V), dims, strides, box,
+            estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+            CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 template <int TPC, int G>
 static void launch_it(const __half* x, __half* V, Args a, long long nrows, unsigned gx,
                       cudaStream_t s) {
   using Gm = Geo<TPC, G>;
-  CUtensorMap map{};
+  CUtensorMap map{}, map_v{};
   int mode = 0;
   size_t smem = Gm::kInSmem + 128;
   if (encode_x_map(&map, x, a.B, a.C, a.H, a.W, Gm::kBoxW, Gm::kCGN) &&
+      encode_v_map(&map_v, V, a.C, a.BP, Gm::kCGN) &&
       smem_optin_once<it_tma_fn<TPC, G>>(Gm::kInSmemTma)) {
-    mode = 1;
+    mode = 1;  // TMA in, TMA out
     smem = Gm::kInSmemTma;
   } else {
     const size_t pair_smem =
@@ -775,21 +854,34 @@ static void launch_it(const __half* x, __half* V, Args a, long long nrows, unsig
     dim3 grid(gx, (unsigned)std::min(kMaxGridY, nrows - done));
     const unsigned thr = 32 * Gm::kWarps;
     if (mode == 1)
-      launch_pdl(kPdlInput, input_transform_fast<TPC, G, 1>, grid, dim3(thr), smem, s, x, V, map, a);
+      launch_pdl(kPdlInput, input_transform_fast<TPC, G, 1>, grid, dim3(thr), smem, s, x, V, map, map_v, a);
     else if (mode == 2)
-      launch_pdl(kPdlInput, input_transform_fast<TPC, G, 2>, grid, dim3(thr), smem, s, x, V, map, a);
+      launch_pdl(kPdlInput, input_transform_fast<TPC, G, 2>, grid, dim3(thr), smem, s, x, V, map, map_v, a);
     else
-      launch_pdl(kPdlInput, input_transform_fast<TPC, G, 0>, grid, dim3(thr), smem, s, x, V, map, a);
+      launch_pdl(kPdlInput, input_transform_fast<TPC, G, 0>, grid, dim3(thr), smem, s, x, V, map, map_v, a);
   }
 }
 
 template <int TPC, int G>
+const void* ot_tma_fn() { return (const void*)output_transform_fast<TPC, G, true>; }
+
+template <int TPC, int G>
 static void launch_ot(const __half* M, __half* y, Args a, long long nrows, unsigned gx,
                       cudaStream_t s) {
+  using Gm = Geo<TPC, G>;
+  CUtensorMap map_m{};
+  const size_t tma_smem = 128 + (size_t)TPC * 64 * Gm::kCGN * 2;
+  const bool tma = encode_v_map(&map_m, M, a.C, a.BP, Gm::kCGN) &&
+                   smem_optin_once<ot_tma_fn<TPC, G>>(tma_smem, 6 * Gm::kOutCols * Gm::kPitch * 2 + 8);
   for (long long done = 0; done < nrows; done += kMaxGridY) {
     a.lrow0 = done;
     dim3 grid(gx, (unsigned)std::min(kMaxGridY, nrows - done));
-    launch_pdl(kPdlOutput, output_transform_fast<TPC, G>, grid, dim3(32 * Geo<TPC, G>::kWarps), 0, s, M, y, a);
+    if (tma)
+      launch_pdl(kPdlOutput, output_transform_fast<TPC, G, true>, grid, dim3(32 * Gm::kWarps),
+                 tma_smem, s, M, y, map_m, a);
+    else
+      launch_pdl(kPdlOutput, output_transform_fast<TPC, G, false>, grid, dim3(32 * Gm::kWarps),
+                 0, s, M, y, map_m, a);
   }
 }
 
