@@ -100,6 +100,8 @@ struct Geo {
   static constexpr int kColPitch = kCGN * 8 + 8;
   static constexpr size_t kInSmemCol = (size_t)kInCols * kColPitch * 2;
   static constexpr size_t kInSmemTma = 128 + kLandBytes + kInSmemCol;
+  // V tiles staged for the TMA stores: [tile][pos][kCGN].
+  static constexpr size_t kVStage = (size_t)TPC * 64 * kCGN * 2;
 };
 
 __device__ __forceinline__ void tma_load_4d(uint32_t dst, const CUtensorMap* map, int c0, int c1,
@@ -143,6 +145,12 @@ __device__ __forceinline__ void block_coords(const Args& a, long long& lrow, int
   th = (int)(grow - (long long)b * a.nh);
 }
 
+template <int TPC, int G>
+__host__ __device__ inline size_t pair_land_bytes(int W) {
+  const size_t pair = (((size_t)Geo<TPC, G>::kCGN * 5 * 2 * W * 2 + 127) / 128) * 128;
+  return pair > Geo<TPC, G>::kVStage ? pair : Geo<TPC, G>::kVStage;
+}
+
 // 16-byte slot of channel c inside a staged column: channels rotate within
 // each octet by the octet index, so the 16-byte reads of 8 consecutive lanes
 // (channels 2l or 2l + 1) fall on 8 different bank groups.
@@ -162,9 +170,11 @@ __global__ void __launch_bounds__(32 * Geo<TPC, G>::kWarps, NOVA_IT_MIN_BLOCKS)
                                                 ~uintptr_t(127));
   // TMA landing buffer [kCGN][8][kBoxW] (TMA path only), then [8][kInCols][kPitch].
   const __half* land = reinterpret_cast<const __half*>(it_base);
+  // The landing buffer also holds the V tiles for the TMA stores once the
+  // staging has been repacked out of it.
   const size_t land_bytes =
       kMode == 1 ? Gm::kLandBytes
-                 : (kMode == 2 ? (((size_t)Gm::kCGN * 5 * 2 * a.W * 2 + 127) / 128) * 128 : 0);
+                 : (kMode == 2 ? pair_land_bytes<TPC, G>(a.W) : 0);
   __half* xs = reinterpret_cast<__half*>(it_base + land_bytes);
   const uint32_t land_s = static_cast<uint32_t>(__cvta_generic_to_shared(land));
   __shared__ uint64_t land_bar;
@@ -346,7 +356,7 @@ __global__ void __launch_bounds__(32 * Geo<TPC, G>::kWarps, NOVA_IT_MIN_BLOCKS)
 #pragma unroll
       for (int i = 0; i < 8; ++i) tt[i][j] = f[i];
     }
-    if constexpr (kMode == 1) {
+    if constexpr (kMode == 1 || kMode == 2) {
       // V tile [pos][kCGN] into the landing buffer, which the repack has freed;
       // channels past C are clipped by the TMA store.
       const uint32_t vrow = land_s + (uint32_t)((t * 64 * Gm::kCGN + cl) * 2);
@@ -375,7 +385,7 @@ __global__ void __launch_bounds__(32 * Geo<TPC, G>::kWarps, NOVA_IT_MIN_BLOCKS)
       }
     }
   }
-  if constexpr (kMode == 1) {
+  if constexpr (kMode == 1 || kMode == 2) {
     tc::fence_async_smem();  // the staged V tiles are visible to the TMA unit
     __syncthreads();
     if (threadIdx.x == 0) {
@@ -840,10 +850,10 @@ static void launch_it(const __half* x, __half* V, Args a, long long nrows, unsig
     mode = 1;  // TMA in, TMA out
     smem = Gm::kInSmemTma;
   } else {
-    const size_t pair_smem =
-        128 + (((size_t)Gm::kCGN * 5 * 2 * a.W * 2 + 127) / 128) * 128 + Gm::kInSmem;
+    const size_t pair_smem = 128 + pair_land_bytes<TPC, G>(a.W) + Gm::kInSmem;
     if (pair_smem <= kPairSmemMax &&
         encode_x_pair_map(&map, x, a.B, a.C, a.H, a.W, Gm::kCGN) &&
+        encode_v_map(&map_v, V, a.C, a.BP, Gm::kCGN) &&
         smem_optin_once<it_pair_fn<TPC, G>>(kPairSmemMax)) {
       mode = 2;
       smem = pair_smem;
