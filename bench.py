@@ -347,7 +347,38 @@ def vendor_layer_times(layers, flush, reps=10):
     return res
 
 
-def roofline_from_stages(stages, peaks):
+# DRAM bytes (read, write) per launch at batch 128, from one ncu capture of the
+# stage entries (profiles/dram_traffic_resnet50_sweep_b128.md gives the command).
+# ncu flushes the caches before each kernel and counts no write-back of lines
+# still dirty in L2 when the kernel ends, so the writes of V and M that stay in
+# the 126 MB L2 are missing here; the totals therefore sit below the algorithmic
+# bytes rather than above them (no kernel re-reads its input).
+NCU_DRAM_BYTES_B128 = {
+    "conv2_x": {"input_transform_kernel": (51410176, 51841536),
+                "gemm_tc_kernel": (105412608, 52168192),
+                "output_transform_kernel": (104875520, 15846656)},
+    "conv3_x": {"input_transform_kernel": (25718272, 2644992),
+                "gemm_tc_kernel": (54556416, 4079360),
+                "output_transform_kernel": (52446208, 89856)},
+    "conv4_x": {"input_transform_kernel": (12878336, 17664),
+                "gemm_tc_kernel": (46167552, 117248),
+                "output_transform_kernel": (37774080, 256)},
+    "conv5_x": {"input_transform_kernel": (6446592, 16384),
+                "gemm_tc_kernel": (67139072, 2708480),
+                "output_transform_kernel": (33575680, 0)},
+}
+
+
+def ncu_traffic(kernel, batch):
+    """Mean DRAM bytes per launch of `kernel` over the sweep layers (ncu), scaled
+    from batch 128 by the tiles processed; None when no capture applies."""
+    vals = [sum(v[kernel]) for v in NCU_DRAM_BYTES_B128.values() if kernel in v]
+    if not vals:
+        return None
+    return sum(vals) / len(vals) * batch / 128.0
+
+
+def roofline_from_stages(stages, peaks, batch=128):
     by_kernel = {}
     for s in stages:
         d = by_kernel.setdefault(s["kernel"], {"ms": 0.0, "bytes": 0.0, "flops": 0.0, "n": 0})
@@ -369,7 +400,9 @@ def roofline_from_stages(stages, peaks):
               "frac": achieved / peaks["hbm_gbs"]}
     tot = sum(x["ms"] for x in by_kernel.values())
     rl.update({"kernel": top, "launches_per_step": d["n"], "avg_launch_ms": d["ms"] / d["n"],
-               "traffic": None, "peak_source": peaks["source"],
+               "traffic": ncu_traffic(top, batch), "traffic_unit": "bytes per launch (ncu)",
+               "algorithmic_bytes_per_launch": d["bytes"] / d["n"],
+               "peak_source": peaks["source"],
                "shares": {k: v["ms"] / tot for k, v in by_kernel.items()}})
     return rl
 
@@ -481,7 +514,7 @@ def run_nova(args):
     stages = roofline = lat = cpu = vendor = None
     if rank == 0:
         stages = stage_profile(layers, batch, flush)
-        roofline = roofline_from_stages(stages, peaks)
+        roofline = roofline_from_stages(stages, peaks, batch)
         lat = b1_latency(device)
         vendor = vendor_layer_times(layers, flush)
         if world == 1 and not args.no_cpu:
