@@ -197,18 +197,30 @@ class NovaWinogradConv2d(nn.Module):
         B, C, H, W = x.shape
         if C != self.in_channels:
             raise ValueError(f"expected {self.in_channels} input channels, got {C}")
-        if x.device != self.weight.device:
+        dev = x.device
+        if dev != self.weight.device:
             raise ValueError("input and weight are on different devices")
-        with torch.cuda.device(x.device):
-            self._ensure_handle()
-            nh, nw, H_out, W_out = self._ensure_workspace(B, H, W)
-            output = torch.empty(B, self.out_channels, H_out, W_out, dtype=torch.float16,
-                                 device=x.device)
-            check(get_lib().nova_forward_workspace_v2(
-                self._handle, ptr(x), ptr(output), ptr(self._V_gemm), ptr(self._M_gemm),
-                B, H, W, self.padding, nh, nw, stream_ptr()), "nova_forward_workspace")
+        if dev.index == torch.cuda.current_device():
+            output = self._launch(x, B, H, W)
+        else:
+            with torch.cuda.device(dev):
+                output = self._launch(x, B, H, W)
         if bias is not None:
             output = output + bias.half().view(1, -1, 1, 1)
+        return output
+
+    def _launch(self, x, B, H, W):
+        """Forward on the current device and stream (the input's device)."""
+        self._ensure_handle()
+        nh, nw, H_out, W_out = self._ensure_workspace(B, H, W)
+        output = torch.empty(B, self.out_channels, H_out, W_out, dtype=torch.float16,
+                             device=x.device)
+        status = get_lib().nova_forward_workspace_v2(
+            self._handle, x.data_ptr(), output.data_ptr(), self._V_gemm.data_ptr(),
+            self._M_gemm.data_ptr(), B, H, W, self.padding, nh, nw,
+            torch.cuda.current_stream().cuda_stream)
+        if status:
+            check(status, "nova_forward_workspace")
         return output
 
     def forward(self, x):

@@ -136,16 +136,26 @@ def check(status, what="nova call"):
     return status
 
 
+_tiling_cache = {}
+
+
 def compute_tiling(H, W, pad):
     """(nh, nw, H_out, W_out) -- the reference's tiling (csrc/nova_winograd.hip:617-631).
 
-    Computed by the library, as in the reference (ops.py:128-144).
+    Computed by the library, as in the reference (ops.py:128-144), once per
+    (H, W, pad): the module classes ask on every forward.
     """
+    key = (int(H), int(W), int(pad))
+    hit = _tiling_cache.get(key)
+    if hit is not None:
+        return hit
     _ensure_lib()
     nh, nw, H_out, W_out = ctypes.c_int(), ctypes.c_int(), ctypes.c_int(), ctypes.c_int()
     _lib.nova_compute_tiling(H, W, pad, ctypes.byref(nh), ctypes.byref(nw),
                              ctypes.byref(H_out), ctypes.byref(W_out))
-    return nh.value, nw.value, H_out.value, W_out.value
+    res = (nh.value, nw.value, H_out.value, W_out.value)
+    _tiling_cache[key] = res
+    return res
 
 
 def create_handle(device=None):
