@@ -253,23 +253,29 @@ __global__ void __launch_bounds__(32 * Geo<TPC, G>::kWarps, NOVA_IT_MIN_BLOCKS)
     constexpr int kChunks = Gm::kBoxW / 8;
     constexpr int kQuads = Gm::kCGN / 4;
     const uint32_t xs_s = static_cast<uint32_t>(__cvta_generic_to_shared(xs));
-    for (int m4 = warp; m4 < kQuads * kChunks; m4 += Gm::kWarps) {
-      const int cq = m4 % kQuads, chunk = m4 / kQuads;
-      const uint32_t src = land_s + (uint32_t)((((cq * 4 + (lane >> 3)) * 8 + (lane & 7)) *
-                                                    Gm::kBoxW + chunk * 8) * 2);
-      uint32_t rg[4];
-      asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0, %1, %2, %3}, [%4];"
-                   : "=r"(rg[0]), "=r"(rg[1]), "=r"(rg[2]), "=r"(rg[3])
-                   : "r"(src)
-                   : "memory");
+    // A warp owns whole 8-column chunks and walks every channel quad of them:
+    // all per-quad offsets (source rows, destination slots) are immediates.
+    const uint32_t src_lane =
+        land_s + (uint32_t)((((lane >> 3) * 8 + (lane & 7)) * Gm::kBoxW) * 2);
+    for (int chunk = warp; chunk < kChunks; chunk += Gm::kWarps) {
       const int col = chunk * 8 + (lane >> 2) - d;
-      if (col >= 0 && col < Gm::kInCols) {
-        const uint32_t dst = xs_s + (uint32_t)((col * Gm::kColPitch + 2 * (lane & 3)) * 2);
+      const bool in = col >= 0 && col < Gm::kInCols;
+      const uint32_t src = src_lane + (uint32_t)(chunk * 16);
+      const uint32_t dst = xs_s + (uint32_t)(((in ? col : 0) * Gm::kColPitch + 2 * (lane & 3)) * 2);
 #pragma unroll
-        for (int i = 0; i < 4; ++i)
-          asm volatile("st.shared.b32 [%0], %1;" ::"r"(dst + (uint32_t)chan_slot(cq * 4 + i) * 16u),
-                       "r"(rg[i])
-                       : "memory");
+      for (int cq = 0; cq < kQuads; ++cq) {
+        uint32_t rg[4];
+        asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0, %1, %2, %3}, [%4];"
+                     : "=r"(rg[0]), "=r"(rg[1]), "=r"(rg[2]), "=r"(rg[3])
+                     : "r"(src + (uint32_t)(cq * 4 * 8 * Gm::kBoxW * 2))
+                     : "memory");
+        if (in) {
+#pragma unroll
+          for (int i = 0; i < 4; ++i)
+            asm volatile("st.shared.b32 [%0], %1;" ::"r"(dst + (uint32_t)chan_slot(cq * 4 + i) * 16u),
+                         "r"(rg[i])
+                         : "memory");
+        }
       }
     }
   } else {
@@ -483,16 +489,22 @@ __global__ void __launch_bounds__(32 * Geo<TPC, G>::kWarps, NOVA_OT_MIN_BLOCKS)
   const int hrows = min(6, H_out - th * 6);
   const long long plane_y = (long long)H_out * W_out;
   __half* yb = y + ((long long)b * K + k0) * plane_y + (long long)(th * 6) * W_out + tw0 * 6;
-  const __half* sbase = ys + lane * Gm::kPitch;
+  // Lane-constant parts once: row offsets in y, validity of the lane's two
+  // columns; the channel loop then only advances two pointers.
   const bool c0ok = lane < wcols, c1ok = lane + 32 < wcols;
-  for (int kl = warp; kl < Gm::kCGN; kl += Gm::kWarps) {
+  int roff[6];
+#pragma unroll
+  for (int r = 0; r < 6; ++r) roff[r] = r < hrows ? r * W_out : -1;
+  const __half* sp = ys + lane * Gm::kPitch + warp;
+  __half* dst = yb + lane + (long long)warp * plane_y;
+  const long long dstep = (long long)Gm::kWarps * plane_y;
+  for (int kl = warp; kl < Gm::kCGN; kl += Gm::kWarps, sp += Gm::kWarps, dst += dstep) {
     if (k0 + kl >= K) break;
-    __half* dst = yb + kl * plane_y;
 #pragma unroll
     for (int r = 0; r < 6; ++r) {
-      if (r < hrows) {
-        if (c0ok) dst[r * W_out + lane] = sbase[r * Gm::kOutCols * Gm::kPitch + kl];
-        if (c1ok) dst[r * W_out + lane + 32] = sbase[(r * Gm::kOutCols + 32) * Gm::kPitch + kl];
+      if (roff[r] >= 0) {
+        if (c0ok) dst[roff[r]] = sp[r * Gm::kOutCols * Gm::kPitch];
+        if (c1ok) dst[roff[r] + 32] = sp[(r * Gm::kOutCols + 32) * Gm::kPitch];
       }
     }
   }
