@@ -210,20 +210,29 @@ __global__ void __launch_bounds__(32 * Geo<TPC, G>::kWarps, NOVA_IT_MIN_BLOCKS)
     if (!mbar_wait_bounded(bar, 0)) return;
     const bool ok0 = lane < Gm::kInCols && w0 + lane >= 0 && w0 + lane < W;
     const bool ok1 = lane + 32 < Gm::kInCols && w0 + lane + 32 >= 0 && w0 + lane + 32 < W;
-    for (int q = warp; q < 8 * (Gm::kCGN / 2); q += Gm::kWarps) {
-      const int r = q & 7, p2 = q >> 3;
+    // Offset of image row h0 + r inside one channel's landing rows, per r.
+    int rowoff[8];
+#pragma unroll
+    for (int r = 0; r < 8; ++r) {
       const int h = h0 + r;
       const int hp = h >= 0 ? h / 2 : -((-h + 1) / 2);
-      const __half* s0 = land + ((2 * p2) * 5 + (hp - p0)) * W2 + (h - 2 * hp) * W + w0;
+      rowoff[r] = (hp - p0) * W2 + (h - 2 * hp) * W + w0 + lane;
+    }
+    const __half z = __ushort_as_half(0);
+    // A warp takes whole channel pairs and walks their 8 rows.
+    for (int p2 = warp; p2 < Gm::kCGN / 2; p2 += Gm::kWarps) {
+      const __half* s0 = land + (2 * p2) * 5 * W2;
       const __half* s1 = s0 + 5 * W2;
-      __half* dst = xs + r * Gm::kInCols * Gm::kPitch + 2 * p2;
-      const __half z = __ushort_as_half(0);
-      if (lane < Gm::kInCols)
-        *reinterpret_cast<__half2*>(dst + lane * Gm::kPitch) =
-            ok0 ? __halves2half2(s0[lane], s1[lane]) : __halves2half2(z, z);
-      if (lane + 32 < Gm::kInCols)
-        *reinterpret_cast<__half2*>(dst + (lane + 32) * Gm::kPitch) =
-            ok1 ? __halves2half2(s0[lane + 32], s1[lane + 32]) : __halves2half2(z, z);
+      __half* dst = xs + lane * Gm::kPitch + 2 * p2;
+#pragma unroll
+      for (int r = 0; r < 8; ++r) {
+        if (lane < Gm::kInCols)
+          *reinterpret_cast<__half2*>(dst + r * Gm::kInCols * Gm::kPitch) =
+              ok0 ? __halves2half2(s0[rowoff[r]], s1[rowoff[r]]) : __halves2half2(z, z);
+        if (lane + 32 < Gm::kInCols)
+          *reinterpret_cast<__half2*>(dst + (r * Gm::kInCols + 32) * Gm::kPitch) =
+              ok1 ? __halves2half2(s0[rowoff[r] + 32], s1[rowoff[r] + 32]) : __halves2half2(z, z);
+      }
     }
   } else if constexpr (kMode == 1) {
     // One TMA tile load brings rows h0..h0+7, columns x0..x0+kBoxW-1 of the
