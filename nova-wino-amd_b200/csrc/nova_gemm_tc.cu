@@ -16,6 +16,7 @@
 //   (2 x BN columns) so the epilogue of tile i overlaps the MMAs of tile i+1.
 // * Every mbarrier wait is bounded (globaltimer); on expiry the kernel records a
 //   status code in device memory, stops issuing work and returns.
+#include <algorithm>
 #include <cstdio>
 #include <cstring>
 
@@ -35,7 +36,8 @@ constexpr int kThreads = 320;   // 10 warps: producer, MMA, 2 epilogue warpgroup
 #endif
 constexpr int kCtasPerSm = NOVA_GEMM_CTAS;       // co-resident CTAs per SM
 constexpr int kTmemCols = 512 / kCtasPerSm;      // each CTA's TMEM share
-constexpr int kMaxBN = kTmemCols / 2 > 128 ? 128 : kTmemCols / 2;  // 2 accumulators
+constexpr int kMaxBN = kTmemCols / 2 > 256 ? 256 : kTmemCols / 2;  // 2 accumulators
+constexpr int kSlabCols = 128;  // epilogue staging: output columns per slab fill
 constexpr int kSmemLimit = (227 * 1024) / kCtasPerSm - (kCtasPerSm > 1 ? 1024 : 0);
 
 struct Params {
@@ -77,7 +79,7 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
   // Epilogue staging: one 32-row slab per epilogue warp, BN/64 chunks of
   // 32 x 128 B in the SWIZZLE_128B layout the M tensor map stores from.
   uint8_t* out_stage = base + (size_t)S * stage_bytes;
-  const uint32_t slab_bytes = p.tma_store ? 32u * (uint32_t)p.BN * 2u : 0u;
+  const uint32_t slab_bytes = p.tma_store ? 32u * (uint32_t)min(p.BN, kSlabCols) * 2u : 0u;
   uint64_t* bars = reinterpret_cast<uint64_t*>(out_stage + 8 * (size_t)slab_bytes);
   uint64_t* full = bars;
   uint64_t* empty = bars + kMaxStages;
@@ -204,34 +206,41 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
       tc_fence_after();
       const uint32_t taddr = tmem_base + ((uint32_t)(q * 32) << 16) + acc * (uint32_t)p.BN;
       if (p.tma_store) {
+        // The slab holds up to kSlabCols columns; wider tiles go out in
+        // kSlabCols-column pieces, each piece's stores read before the next fill.
         uint8_t* slab = out_stage + (eg * 4 + q) * slab_bytes;
-        if (lane == 0) bulk_wait_read_all();  // the previous tile's store has read the slab
-        __syncwarp();
         uint8_t* my_row = slab + lane * 128;
-        for (int j = 0; j < p.BN; j += 32) {
-          uint32_t r[32];
-          tmem_ld32(taddr + j, r);
-          uint8_t* chunk_row = my_row + (j >> 6) * 4096;
-          const int c_base = (j & 63) >> 3;  // first 16-byte chunk of these 32 columns
+        for (int h0 = 0; h0 < p.BN; h0 += kSlabCols) {
+          const int h1 = min(p.BN, h0 + kSlabCols);
+          if (lane == 0) bulk_wait_read_all();  // earlier stores have read the slab
+          __syncwarp();
+          for (int j = h0; j < h1; j += 32) {
+            uint32_t r[32];
+            tmem_ld32(taddr + j, r);
+            uint8_t* chunk_row = my_row + ((j - h0) >> 6) * 4096;
+            const int c_base = (j & 63) >> 3;  // first 16-byte chunk of these 32 columns
 #pragma unroll
-          for (int v = 0; v < 4; ++v) {
-            uint4 w;
-            w.x = pack_half2(r[8 * v + 0], r[8 * v + 1]);
-            w.y = pack_half2(r[8 * v + 2], r[8 * v + 3]);
-            w.z = pack_half2(r[8 * v + 4], r[8 * v + 5]);
-            w.w = pack_half2(r[8 * v + 6], r[8 * v + 7]);
-            *reinterpret_cast<uint4*>(chunk_row + (((c_base + v) ^ (lane & 7)) << 4)) = w;
+            for (int v = 0; v < 4; ++v) {
+              uint4 w;
+              w.x = pack_half2(r[8 * v + 0], r[8 * v + 1]);
+              w.y = pack_half2(r[8 * v + 2], r[8 * v + 3]);
+              w.z = pack_half2(r[8 * v + 4], r[8 * v + 5]);
+              w.w = pack_half2(r[8 * v + 6], r[8 * v + 7]);
+              *reinterpret_cast<uint4*>(chunk_row + (((c_base + v) ^ (lane & 7)) << 4)) = w;
+            }
           }
-        }
-        tc_fence_before();
-        mbar_arrive(smem_u32(&tempty[acc]));  // TMEM is free once read
-        fence_async_smem();
-        __syncwarp();
-        if (lane == 0) {
-          for (int jc = 0; jc < p.BN / 64; ++jc)
-            tma_store_3d(&tmM, smem_u32(slab + jc * 4096), kt * p.BN + jc * 64,
-                         bpt * kBM + q * 32, pos);
-          bulk_commit();
+          if (h1 == p.BN) {
+            tc_fence_before();
+            mbar_arrive(smem_u32(&tempty[acc]));  // TMEM is free once read
+          }
+          fence_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            for (int jc = 0; jc < (h1 - h0) / 64; ++jc)
+              tma_store_3d(&tmM, smem_u32(slab + jc * 4096), kt * p.BN + h0 + jc * 64,
+                           bpt * kBM + q * 32, pos);
+            bulk_commit();
+          }
         }
         continue;
       }
@@ -375,7 +384,7 @@ cudaError_t tc_gemm_run(const TcGemmPlan& plan, const __half* V, __half* M, long
   p.total_tiles = 64ll * p.n_bp_tiles * p.n_k_tiles;
   p.status = dev_status;
   const int stage_bytes = tc::kBM * tc::kBK * 2 + plan.BN * tc::kBK * 2;
-  const int out_bytes = p.tma_store ? 8 * 32 * plan.BN * 2 : 0;
+  const int out_bytes = p.tma_store ? 8 * 32 * std::min(plan.BN, tc::kSlabCols) * 2 : 0;
   const int overhead = 1024 + 256 + out_bytes;
   p.stages = (tc::kSmemLimit - overhead) / stage_bytes;
   if (p.stages > tc::kMaxStages) p.stages = tc::kMaxStages;
