@@ -184,6 +184,47 @@ def test_batch_consistency_bit_exact():
         np.testing.assert_array_equal(yb[b:b + 1], yi)
 
 
+def test_plane_launch_shapes_agree():
+    # 14x14 images are 3x3 tiles.  At batch 40 with 256 channels, 160 blocks
+    # of 64 channels take the throughput plane kernels (3-warp input
+    # transform).  A single image takes the one-warp-per-tile kernels.  Same
+    # arithmetic per tile, so the outputs are bit-identical.
+    x, w = o.synthetic_case(40, 256, 256, 14, 14, seed=404)
+    yb, _ = run_forward(x, w, 1, path=1)
+    for b in (0, 17, 39):
+        yi, _ = run_forward(x[b:b + 1], w, 1, path=1)
+        np.testing.assert_array_equal(yb[b:b + 1], yi)
+    check_parity(x[:2], w, 1, yb[:2])
+
+
+def test_programmatic_launch_off_matches_default():
+    # The same forward in a child process with programmatic dependent launch
+    # disabled (NOVA_PDL_MASK=0) writes the same bytes.
+    import os
+    import subprocess
+    import sys
+    import tempfile
+    x, w = o.synthetic_case(3, 64, 128, 30, 30, seed=505)
+    y, _ = run_forward(x, w, 1)
+    here = os.path.dirname(os.path.abspath(__file__))
+    root = os.path.dirname(here)
+    with tempfile.TemporaryDirectory() as tmp:
+        np.save(os.path.join(tmp, "x.npy"), x)
+        np.save(os.path.join(tmp, "w.npy"), w)
+        code = (
+            "import sys, numpy as np\n"
+            f"sys.path[:0] = [{os.path.join(root, 'nova-wino-amd_b200')!r}, {here!r}, "
+            f"{os.path.join(root, 'oracle')!r}]\n"
+            "from test_gpu_parity import run_forward\n"
+            f"x = np.load({os.path.join(tmp, 'x.npy')!r}); w = np.load({os.path.join(tmp, 'w.npy')!r})\n"
+            "y, _ = run_forward(x, w, 1)\n"
+            f"np.save({os.path.join(tmp, 'y.npy')!r}, y)\n")
+        env = dict(os.environ, NOVA_PDL_MASK="0")
+        subprocess.run([sys.executable, "-c", code], check=True, env=env, timeout=600)
+        y0 = np.load(os.path.join(tmp, "y.npy"))
+    np.testing.assert_array_equal(y, y0)
+
+
 def test_empty_batch_is_a_no_op():
     L = lib()
     w = torch.randn(16, 8, 3, 3, device="cuda")
