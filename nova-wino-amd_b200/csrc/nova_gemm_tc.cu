@@ -349,6 +349,9 @@ cudaError_t tc_gemm_plan(TcGemmPlan* plan, const __half* U, int K, int C, const 
     *why = "cuTensorMapEncodeTiled failed for U";
     return cudaErrorInvalidValue;
   }
+  // Narrower tiles for launches too small to fill the GPU with wide ones.
+  plan->has_half = plan->BN > 128 && (plan->BN / 2) % 16 == 0 &&
+                   tc::encode_operand_map(&plan->tmU_half, U, C, K, plan->BN / 2);
   plan->valid = true;
   return cudaSuccess;
 }
@@ -369,22 +372,33 @@ cudaError_t tc_gemm_run(const TcGemmPlan& plan, const __half* V, __half* M, long
     *why = "cuTensorMapEncodeTiled failed for V";
     return cudaErrorInvalidValue;
   }
+  // Tile width: BN, or BN/2 when BN-wide tiles would leave more than half of
+  // the SMs idle (batch-1 shapes), so the launch spreads over more CTAs.
+  int BN = plan.BN;
+  const CUtensorMap* tmU = &plan.tmU;
+  {
+    const long long n_bp = (BP + tc::kBM - 1) / tc::kBM;
+    if (plan.has_half && 64ll * n_bp * (plan.K / plan.BN) * 2 <= num_sms) {
+      BN = plan.BN / 2;
+      tmU = &plan.tmU_half;
+    }
+  }
   tc::Params p;
   CUtensorMap tmM;
-  p.tma_store = (plan.BN % 64) == 0 &&
+  p.tma_store = (BN % 64) == 0 &&
                 tc::encode_operand_map(&tmM, M, plan.K, BP, 32);
   p.M = M;
   p.BP = BP;
   p.C = plan.C;
   p.K = plan.K;
-  p.BN = plan.BN;
+  p.BN = BN;
   p.n_bp_tiles = (int)((BP + tc::kBM - 1) / tc::kBM);
-  p.n_k_tiles = plan.K / plan.BN;
+  p.n_k_tiles = plan.K / BN;
   p.n_cblk = (plan.C + tc::kBK - 1) / tc::kBK;
   p.total_tiles = 64ll * p.n_bp_tiles * p.n_k_tiles;
   p.status = dev_status;
-  const int stage_bytes = tc::kBM * tc::kBK * 2 + plan.BN * tc::kBK * 2;
-  const int out_bytes = p.tma_store ? 8 * 32 * std::min(plan.BN, tc::kSlabCols) * 2 : 0;
+  const int stage_bytes = tc::kBM * tc::kBK * 2 + BN * tc::kBK * 2;
+  const int out_bytes = p.tma_store ? 8 * 32 * std::min(BN, tc::kSlabCols) * 2 : 0;
   const int overhead = 1024 + 256 + out_bytes;
   p.stages = (tc::kSmemLimit - overhead) / stage_bytes;
   if (p.stages > tc::kMaxStages) p.stages = tc::kMaxStages;
@@ -409,7 +423,7 @@ cudaError_t tc_gemm_run(const TcGemmPlan& plan, const __half* V, __half* M, long
   const long long slots = (long long)num_sms * tc::kCtasPerSm;
   long long grid = p.total_tiles < slots ? p.total_tiles : slots;
   cudaError_t e = launch_pdl(kPdlGemm, tc::gemm_tc_kernel, dim3((unsigned)grid), dim3(tc::kThreads), smem, s,
-                             tmV, plan.tmU, tmM, p);
+                             tmV, *tmU, tmM, p);
   if (e != cudaSuccess) *why = "tensor-core GEMM launch failed";
   return e;
 }

@@ -76,9 +76,11 @@ cudaError_t launch_gemm_simt(const __half* V, const __half* U, __half* M, long l
 
 // Tensor-core (tcgen05 + TMA) batched GEMM.
 struct TcGemmPlan {
-  CUtensorMap tmU;  // U internal layout [64][K][C], box {64 c, BN k, 1}
-  int BN = 0;       // output channels per tile (MMA N)
+  CUtensorMap tmU;       // U internal layout [64][K][C], box {64 c, BN k, 1}
+  CUtensorMap tmU_half;  // the same with box {64 c, BN/2 k, 1} (BN > 128 only)
+  int BN = 0;            // output channels per tile (MMA N)
   int K = 0, C = 0;
+  bool has_half = false;
   bool valid = false;
 };
 
