@@ -354,18 +354,18 @@ def vendor_layer_times(layers, flush, reps=10):
 # the 126 MB L2 are missing here; the totals therefore sit below the algorithmic
 # bytes rather than above them (no kernel re-reads its input).
 NCU_DRAM_BYTES_B128 = {
-    "conv2_x": {"input_transform_kernel": (51403776, 51991296),
-                "gemm_tc_kernel": (105412608, 52209664),
-                "output_transform_kernel": (104875264, 15716352)},
-    "conv3_x": {"input_transform_kernel": (25715456, 971008),
-                "gemm_tc_kernel": (54556672, 4330496),
-                "output_transform_kernel": (52446208, 125952)},
-    "conv4_x": {"input_transform_kernel": (12872704, 17152),
-                "gemm_tc_kernel": (46167296, 133376),
-                "output_transform_kernel": (37774336, 512)},
-    "conv5_x": {"input_transform_kernel": (6446592, 16896),
-                "gemm_tc_kernel": (67139072, 3101184),
-                "output_transform_kernel": (33575424, 0)},
+    "conv2_x": {"input_transform_kernel": (51408896, 52868608),
+                "gemm_tc_kernel": (105416192, 52318720),
+                "output_transform_kernel": (104876544, 16097280)},
+    "conv3_x": {"input_transform_kernel": (25714176, 788224),
+                "gemm_tc_kernel": (54556928, 4594432),
+                "output_transform_kernel": (52446464, 57344)},
+    "conv4_x": {"input_transform_kernel": (12876288, 6656),
+                "gemm_tc_kernel": (46167552, 53760),
+                "output_transform_kernel": (37768192, 0)},
+    "conv5_x": {"input_transform_kernel": (6447872, 16384),
+                "gemm_tc_kernel": (67140096, 997376),
+                "output_transform_kernel": (33570560, 0)},
 }
 
 
