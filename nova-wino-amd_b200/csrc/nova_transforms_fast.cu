@@ -114,6 +114,15 @@ __device__ __forceinline__ void tma_load_4d(uint32_t dst, const CUtensorMap* map
       : "memory");
 }
 
+__device__ __forceinline__ void tma_store_4d(const CUtensorMap* map, uint32_t src, int c0, int c1,
+                                             int c2, int c3) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.global.shared::cta.bulk_group [%0, {%1, %2, %3, %4}], [%5];" ::"l"(
+          reinterpret_cast<uint64_t>(map)),
+      "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(src)
+      : "memory");
+}
+
 // Bounded mbarrier wait (2 s of globaltimer); false on expiry.
 __device__ __forceinline__ bool mbar_wait_bounded(uint32_t bar, uint32_t parity) {
   uint64_t t0 = 0;
@@ -422,12 +431,18 @@ __global__ void __launch_bounds__(32 * Geo<TPC, G>::kWarps, NOVA_IT_MIN_BLOCKS)
 
 // kTmaIn: the block's M tiles ([pos][channels] each) arrive by TMA tile loads
 // into shared memory instead of 64 scattered 4-byte loads per lane.
-template <int TPC, int G, bool kTmaIn>
+// kYTma (needs kTmaIn; W_out % 8 == 0 and TPC = 4, so every chunk starts on a
+// 48-byte boundary): the staged 6 x 6*TPC output rows are transposed with
+// ldmatrix.trans into a dense [channel][row][col] box in the freed M buffer
+// and leave by one TMA tile store per block.
+template <int TPC, int G, bool kTmaIn, bool kYTma = false>
 __global__ void __launch_bounds__(32 * Geo<TPC, G>::kWarps, NOVA_OT_MIN_BLOCKS)
     output_transform_fast(const __half* __restrict__ M, __half* __restrict__ y,
-                          const __grid_constant__ CUtensorMap map_m, const Args a) {
+                          const __grid_constant__ CUtensorMap map_m,
+                          const __grid_constant__ CUtensorMap map_y, const Args a) {
   using Gm = Geo<TPC, G>;
-  __shared__ __align__(16) __half ys[6 * Gm::kOutCols * Gm::kPitch];
+  constexpr int kYP = kYTma ? Gm::kCGN + 8 : Gm::kPitch;  // halves per staged pixel
+  __shared__ __align__(16) __half ys[6 * Gm::kOutCols * kYP];
   extern __shared__ uint8_t ot_raw[];
   __shared__ uint64_t m_bar;
   long long lrow;
@@ -488,11 +503,50 @@ __global__ void __launch_bounds__(32 * Geo<TPC, G>::kWarps, NOVA_OT_MIN_BLOCKS)
       a_1d2(tt[i], g);
 #pragma unroll
       for (int j = 0; j < 6; ++j)
-        *reinterpret_cast<__half2*>(ys + (i * Gm::kOutCols + t * 6 + j) * Gm::kPitch + kl) =
+        *reinterpret_cast<__half2*>(ys + (i * Gm::kOutCols + t * 6 + j) * kYP + kl) =
             __float22half2_rn(g[j]);
     }
   }
   __syncthreads();
+
+  if constexpr (kYTma) {
+    static_assert(kTmaIn && Gm::kOutCols % 8 == 0, "dense y box needs the M buffer and 8-col groups");
+    constexpr int kGroups = Gm::kOutCols / 8;
+    constexpr int kQuads = Gm::kCGN / 32;
+    const uint32_t ys_s = static_cast<uint32_t>(__cvta_generic_to_shared(ys));
+    const uint32_t yd_s = static_cast<uint32_t>(__cvta_generic_to_shared(mtiles));
+    // Lane L addresses pixel L%8 of channel octet L/8 of an 8-pixel x 32-channel
+    // block and receives pixels 2(L%4), 2(L%4)+1 of channel L/4 of each octet.
+    const uint32_t lane_src = ys_s + (uint32_t)(((lane & 7) * kYP + (lane >> 3) * 8) * 2);
+    const uint32_t lane_dst = yd_s + (uint32_t)(((lane >> 2) * 6 * Gm::kOutCols + 2 * (lane & 3)) * 2);
+    for (int item = warp; item < 6 * kGroups * kQuads; item += Gm::kWarps) {
+      const int r = item / (kGroups * kQuads);
+      const int rem = item - r * (kGroups * kQuads);
+      const int g = rem / kQuads, o4 = rem - (rem / kQuads) * kQuads;
+      uint32_t rg[4];
+      asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0, %1, %2, %3}, [%4];"
+                   : "=r"(rg[0]), "=r"(rg[1]), "=r"(rg[2]), "=r"(rg[3])
+                   : "r"(lane_src + (uint32_t)(((r * Gm::kOutCols + 8 * g) * kYP + o4 * 32) * 2))
+                   : "memory");
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+        asm volatile("st.shared.b32 [%0], %1;" ::"r"(
+                         lane_dst + (uint32_t)((((o4 * 32 + 8 * i) * 6 + r) * Gm::kOutCols + 8 * g) * 2)),
+                     "r"(rg[i])
+                     : "memory");
+    }
+    tc::fence_async_smem();  // the dense box is visible to the TMA unit
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      // Rows past H_out, columns past W_out and channels past K are clipped.
+      tma_store_4d(&map_y, yd_s, tw0 * 6, th * 6, k0, b);
+      tc::bulk_commit();
+      tc::bulk_wait_read_all();
+    }
+    __syncthreads();
+    pdl_trigger();  // after the whole block is done
+    return;
+  }
 
   // Write output rows: warp per channel (6 rows each), lane per column.
   const int wcols = min(ntw * 6, W_out - tw0 * 6);
@@ -505,7 +559,7 @@ __global__ void __launch_bounds__(32 * Geo<TPC, G>::kWarps, NOVA_OT_MIN_BLOCKS)
   int roff[6];
 #pragma unroll
   for (int r = 0; r < 6; ++r) roff[r] = r < hrows ? r * W_out : -1;
-  const __half* sp = ys + lane * Gm::kPitch + warp;
+  const __half* sp = ys + lane * kYP + warp;
   __half* dst = yb + lane + (long long)warp * plane_y;
   const long long dstep = (long long)Gm::kWarps * plane_y;
   for (int kl = warp; kl < Gm::kCGN; kl += Gm::kWarps, sp += Gm::kWarps, dst += dstep) {
@@ -513,8 +567,8 @@ __global__ void __launch_bounds__(32 * Geo<TPC, G>::kWarps, NOVA_OT_MIN_BLOCKS)
 #pragma unroll
     for (int r = 0; r < 6; ++r) {
       if (roff[r] >= 0) {
-        if (c0ok) dst[roff[r]] = sp[r * Gm::kOutCols * Gm::kPitch];
-        if (c1ok) dst[roff[r] + 32] = sp[(r * Gm::kOutCols + 32) * Gm::kPitch];
+        if (c0ok) dst[roff[r]] = sp[r * Gm::kOutCols * kYP];
+        if (c1ok) dst[roff[r] + 32] = sp[(r * Gm::kOutCols + 32) * kYP];
       }
     }
   }
@@ -963,6 +1017,31 @@ static void launch_it(const __half* x, __half* V, Args a, long long nrows, unsig
 
 template <int TPC, int G>
 const void* ot_tma_fn() { return (const void*)output_transform_fast<TPC, G, true>; }
+const void* ot_ytma_fn() { return (const void*)output_transform_fast<4, 1, true, true>; }
+
+// y as [B][K][H_out][W_out] (W fastest), box {24, 6, 64, 1}: one TMA store per
+// 4-tile chunk.  Needs W_out % 8 == 0 (16-byte row stride).
+static bool encode_y_map(CUtensorMap* map, const __half* y, int B, int K, int H_out, int W_out) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn || (W_out % 8) || (reinterpret_cast<uintptr_t>(y) & 15)) return false;
+  cuuint64_t dims[4] = {(cuuint64_t)W_out, (cuuint64_t)H_out, (cuuint64_t)K, (cuuint64_t)B};
+  cuuint64_t strides[3] = {(cuuint64_t)W_out * 2, (cuuint64_t)H_out * W_out * 2,
+                           (cuuint64_t)K * H_out * W_out * 2};
+  cuuint32_t box[4] = {24, 6, 64, 1};
+  cuuint32_t estr[4] = {1, 1, 1, 1};
+  return fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4, const_cast<__half*>(y), dims, strides, box,
+            estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+            CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// The TMA y-store output transform, on unless NOVA_OT_YTMA=0.
+static bool ot_ytma_enabled() {
+  static const bool on = [] {
+    const char* e = std::getenv("NOVA_OT_YTMA");
+    return !(e && e[0] == '0');
+  }();
+  return on;
+}
 
 template <int TPC, int G>
 static void launch_ot(const __half* M, __half* y, Args a, long long nrows, unsigned gx,
@@ -977,10 +1056,10 @@ static void launch_ot(const __half* M, __half* y, Args a, long long nrows, unsig
     dim3 grid(gx, (unsigned)std::min(kMaxGridY, nrows - done));
     if (tma)
       launch_pdl(kPdlOutput, output_transform_fast<TPC, G, true>, grid, dim3(32 * Gm::kWarps),
-                 tma_smem, s, M, y, map_m, a);
+                 tma_smem, s, M, y, map_m, map_m, a);
     else
       launch_pdl(kPdlOutput, output_transform_fast<TPC, G, false>, grid, dim3(32 * Gm::kWarps),
-                 0, s, M, y, map_m, a);
+                 0, s, M, y, map_m, map_m, a);
   }
 }
 
@@ -1033,6 +1112,27 @@ cudaError_t launch_output_transform_fast(const __half* M, __half* y, int K, int 
     NOVA_PLANE_SWITCH(nh, nw, fast::launch_ot_plane, M, y, a, nrows / nh,
                       (unsigned)((K + 63) / 64), s);
     return cudaGetLastError();
+  }
+  if ((W_out % 8) == 0 && nw >= 4 && fast::ot_ytma_enabled()) {
+    // 4-tile chunks, 64 channels per block, y out by TMA tile stores.
+    using Gm = fast::Geo<4, 1>;
+    const int B_imgs = (int)((row0 + nrows + nh - 1) / nh);
+    CUtensorMap map_m{}, map_y{};
+    const size_t tma_smem = 128 + (size_t)4 * 64 * 64 * 2;
+    if (fast::encode_v_map(&map_m, M, K, BP, 64) &&
+        fast::encode_y_map(&map_y, y, B_imgs, K, H_out, W_out) &&
+        fast::smem_optin_once<fast::ot_ytma_fn>(tma_smem, 6 * Gm::kOutCols * (Gm::kCGN + 8) * 2 + 8)) {
+      const int n_twc = (nw + 3) / 4;
+      fast::Args a{K, H_out, W_out, 0, 0, nh, nw, row0, 0, BP, n_twc};
+      const unsigned gx = (unsigned)(n_twc * ((K + 63) / 64));
+      for (long long done = 0; done < nrows; done += fast::kMaxGridY) {
+        a.lrow0 = done;
+        dim3 grid(gx, (unsigned)std::min(fast::kMaxGridY, nrows - done));
+        launch_pdl(kPdlOutput, fast::output_transform_fast<4, 1, true, true>, grid,
+                   dim3(32 * Gm::kWarps), tma_smem, s, M, y, map_m, map_y, a);
+      }
+      return cudaGetLastError();
+    }
   }
   const fast::Plan p = fast::make_plan(nw, K);
   fast::Args a{K, H_out, W_out, 0, 0, nh, nw, row0, 0, BP, p.n_twc};
