@@ -642,6 +642,15 @@ def profile_stages(args):
     y = torch.empty(args.batch, C, H, H, dtype=torch.float16, device="cuda")
     conv(x)
     s = ops.stream_ptr()
+    if args.fused:
+        # The fused single kernel (path 3) on the same layer, --steps times.
+        ops.check(lib.nova_set_path(conv._handle, ops.PATH_FUSED), "set_path(fused)")
+        for _ in range(args.steps):
+            ops.check(lib.nova_forward_v2(conv._handle, ops.ptr(x), ops.ptr(y), args.batch, H, H,
+                                          1, s), "fused forward")
+        torch.cuda.synchronize()
+        print(f"profile-stages {name} batch {args.batch} (fused): ok")
+        return
     for _ in range(args.steps):
         ops.check(lib.nova_input_transform_v2(ops.ptr(x), ops.ptr(V), args.batch, C, H, H, 1,
                                               nt, nt, BP, s), "input_transform")
@@ -679,6 +688,8 @@ def main():
     ap.add_argument("--workload", choices=["sweep", "resnet50"], default="sweep",
                     help="sweep: ResNet-50 3x3 layer sweep (BASELINE config 2, default); "
                          "resnet50: whole model images/s (config 3)")
+    ap.add_argument("--fused", action="store_true",
+                    help="with --profile-stages: run the fused single kernel instead (C, K <= 64)")
     ap.add_argument("--profile-stages", metavar="LAYER", default=None,
                     help="only run the three stage entries of one sweep layer (--steps times "
                          "each, no timing output): the driver for ncu captures")

@@ -37,7 +37,7 @@ constexpr int kThreads = 320;   // 10 warps: producer, MMA, 2 epilogue warpgroup
 constexpr int kCtasPerSm = NOVA_GEMM_CTAS;       // co-resident CTAs per SM
 constexpr int kTmemCols = 512 / kCtasPerSm;      // each CTA's TMEM share
 constexpr int kMaxBN = kTmemCols / 2 > 256 ? 256 : kTmemCols / 2;  // 2 accumulators
-constexpr int kSlabCols = 128;  // epilogue staging: output columns per slab fill
+constexpr int kSlabCols = 64;   // epilogue staging: output columns per slab fill
 constexpr int kSmemLimit = (227 * 1024) / kCtasPerSm - (kCtasPerSm > 1 ? 1024 : 0);
 
 struct Params {
