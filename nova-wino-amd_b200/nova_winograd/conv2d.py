@@ -124,6 +124,14 @@ class NovaWinogradFunction(torch.autograd.Function):
 # Inference module (reference conv2d.py:154-273)
 # ---------------------------------------------------------------------------
 
+def _raw_stream(device_index):
+    """cudaStream_t of the current stream on device_index, as an int."""
+    get = getattr(torch._C, "_cuda_getCurrentRawStream", None)
+    if get is not None:
+        return get(device_index)
+    return torch.cuda.current_stream(device_index).cuda_stream
+
+
 class NovaWinogradConv2d(nn.Module):
     """Drop-in replacement for nn.Conv2d (3x3, stride 1) using NOVA F(6,3).
 
@@ -151,6 +159,7 @@ class NovaWinogradConv2d(nn.Module):
         self._V_gemm = None
         self._M_gemm = None
         self._last_config = None
+        self._fast = None
 
     def _ensure_handle(self):
         """Create the native context and refresh U when the weights changed."""
@@ -191,6 +200,20 @@ class NovaWinogradConv2d(nn.Module):
         return nh, nw, H_out, W_out
 
     def _native_forward(self, x, bias):
+        # Steady state: same input geometry and device, same weight tensor and
+        # version as the call that filled _fast -- skip straight to the launch.
+        fast = self._fast
+        if (fast is not None and fast[0] == x.shape and fast[1] == x.device
+                and fast[2] == self.weight._version and fast[3] == self.weight.data_ptr()
+                and fast[4] == torch.cuda.current_device()):
+            output = torch.empty(fast[5], dtype=torch.float16, device=x.device)
+            status = fast[6](self._handle, x.data_ptr(), output.data_ptr(), fast[7], fast[8],
+                             *fast[9], _raw_stream(fast[4]))
+            if status:
+                check(status, "nova_forward_workspace")
+            if bias is not None:
+                output = output + bias.half().view(1, -1, 1, 1)
+            return output
         _ensure_lib()
         if not x.is_cuda:
             raise ValueError("input must be a CUDA tensor")
@@ -215,12 +238,15 @@ class NovaWinogradConv2d(nn.Module):
         nh, nw, H_out, W_out = self._ensure_workspace(B, H, W)
         output = torch.empty(B, self.out_channels, H_out, W_out, dtype=torch.float16,
                              device=x.device)
-        status = get_lib().nova_forward_workspace_v2(
-            self._handle, x.data_ptr(), output.data_ptr(), self._V_gemm.data_ptr(),
-            self._M_gemm.data_ptr(), B, H, W, self.padding, nh, nw,
-            torch.cuda.current_stream().cuda_stream)
+        fn = get_lib().nova_forward_workspace_v2
+        ints = (B, H, W, self.padding, nh, nw)
+        status = fn(self._handle, x.data_ptr(), output.data_ptr(), self._V_gemm.data_ptr(),
+                    self._M_gemm.data_ptr(), *ints, _raw_stream(x.device.index))
         if status:
             check(status, "nova_forward_workspace")
+        self._fast = (x.shape, x.device, self.weight._version, self.weight.data_ptr(),
+                      x.device.index, tuple(output.shape), fn, self._V_gemm.data_ptr(),
+                      self._M_gemm.data_ptr(), ints)
         return output
 
     def forward(self, x):
