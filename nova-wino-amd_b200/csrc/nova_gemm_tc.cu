@@ -302,8 +302,16 @@ static EncodeTiledFn get_encode_fn() {
 }
 
 // 3-D FP16 map over [64][rows][C] (C fastest), box {64, box_rows, 1}, SWIZZLE_128B.
+static bool encode_operand_map_raw(CUtensorMap* map, const void* ptr, int C, long long rows,
+                                   int box_rows);
 static bool encode_operand_map(CUtensorMap* map, const void* ptr, int C, long long rows,
                                int box_rows) {
+  return cached_tensor_map(map, ptr, C, rows, box_rows, 2, [&](CUtensorMap* m) {
+    return encode_operand_map_raw(m, ptr, C, rows, box_rows);
+  });
+}
+static bool encode_operand_map_raw(CUtensorMap* map, const void* ptr, int C, long long rows,
+                                   int box_rows) {
   EncodeTiledFn fn = get_encode_fn();
   if (!fn) return false;
   cuuint64_t dims[3] = {(cuuint64_t)C, (cuuint64_t)rows, 64};

@@ -14,6 +14,34 @@
 
 namespace nova {
 
+// Per-thread cache of encoded TMA descriptors.  A descriptor depends only on
+// the base address, the dims / strides and the box, all of which are in the
+// key, so a hit is always the descriptor a fresh encode would produce.  The
+// workspaces (V, M) keep their addresses across calls, which saves their
+// host-side encodes on every forward.
+template <typename Encode>
+bool cached_tensor_map(CUtensorMap* map, const void* ptr, long long k0, long long k1,
+                       long long k2, int tag, Encode&& encode) {
+  struct Entry {
+    const void* ptr;
+    long long k0, k1, k2;
+    int tag;
+    CUtensorMap map;
+  };
+  constexpr int kEntries = 16;
+  thread_local Entry cache[kEntries] = {};
+  thread_local int next = 0;
+  for (const Entry& e : cache)
+    if (e.ptr == ptr && ptr != nullptr && e.k0 == k0 && e.k1 == k1 && e.k2 == k2 && e.tag == tag) {
+      *map = e.map;
+      return true;
+    }
+  if (!encode(map)) return false;
+  cache[next] = Entry{ptr, k0, k1, k2, tag, *map};
+  next = (next + 1) % kEntries;
+  return true;
+}
+
 // Programmatic dependent launch for the hot-path kernels.  Kinds: 1 = input
 // transform, 2 = tensor-core GEMM, 4 = output transform, 8 = fused kernel;
 // NOVA_PDL_MASK (default: all) selects which kinds launch with it.  The kernel

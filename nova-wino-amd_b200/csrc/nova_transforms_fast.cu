@@ -929,7 +929,7 @@ static EncodeTiledFn encode_fn() {
 
 // 4-D map over x [B][C][H][W] (W fastest) with box {box_w, 8, cgn, 1}; needs
 // W % 8 == 0 (16-byte row stride) and a 16-byte aligned base.
-static bool encode_x_map(CUtensorMap* map, const __half* x, int B, int C, int H, int W,
+static bool encode_x_map_raw(CUtensorMap* map, const __half* x, int B, int C, int H, int W,
                          int box_w, int cgn) {
   EncodeTiledFn fn = encode_fn();
   if (!fn || (W % 8) || (reinterpret_cast<uintptr_t>(x) & 15)) return false;
@@ -942,6 +942,13 @@ static bool encode_x_map(CUtensorMap* map, const __half* x, int B, int C, int H,
             CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+static bool encode_x_map(CUtensorMap* map, const __half* x, int B, int C, int H, int W,
+                         int box_w, int cgn) {
+  return cached_tensor_map(map, x, ((long long)B << 32) | (unsigned)C, ((long long)H << 32) | (unsigned)W, ((long long)box_w << 32) | (unsigned)cgn, 3, [&](CUtensorMap* m) {
+    return encode_x_map_raw(m, x, B, C, H, W, box_w, cgn);
+  });
+}
+
 template <int TPC, int G>
 const void* it_tma_fn() { return (const void*)input_transform_fast<TPC, G, 1>; }
 template <int TPC, int G>
@@ -950,7 +957,7 @@ const void* it_pair_fn() { return (const void*)input_transform_fast<TPC, G, 2>; 
 constexpr size_t kPairSmemMax = 100 * 1024;
 
 // Pair-row view of x: dims {2W, H/2, C, B}, box {2W, 5, cgn, 1}.
-static bool encode_x_pair_map(CUtensorMap* map, const __half* x, int B, int C, int H, int W,
+static bool encode_x_pair_map_raw(CUtensorMap* map, const __half* x, int B, int C, int H, int W,
                               int cgn) {
   EncodeTiledFn fn = encode_fn();
   if (!fn || (W % 4) || (H % 2) || 2 * W > 256 || (reinterpret_cast<uintptr_t>(x) & 15))
@@ -964,9 +971,16 @@ static bool encode_x_pair_map(CUtensorMap* map, const __half* x, int B, int C, i
             CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+static bool encode_x_pair_map(CUtensorMap* map, const __half* x, int B, int C, int H, int W,
+                              int cgn) {
+  return cached_tensor_map(map, x, ((long long)B << 32) | (unsigned)C, ((long long)H << 32) | (unsigned)W, cgn, 4, [&](CUtensorMap* m) {
+    return encode_x_pair_map_raw(m, x, B, C, H, W, cgn);
+  });
+}
+
 // V as [64 pos][BP][C] (C fastest), box {cgn, 1 tile, 64 pos}: one TMA store
 // per staged tile.  Needs C % 8 == 0 (16-byte strides) and BP < 2^31.
-static bool encode_v_map(CUtensorMap* map, const __half* V, int C, long long BP, int cgn) {
+static bool encode_v_map_raw(CUtensorMap* map, const __half* V, int C, long long BP, int cgn) {
   EncodeTiledFn fn = encode_fn();
   if (!fn || (C % 8) || BP <= 0 || BP >= (1ll << 31) ||
       (reinterpret_cast<uintptr_t>(V) & 15))
@@ -978,6 +992,12 @@ static bool encode_v_map(CUtensorMap* map, const __half* V, int C, long long BP,
   return fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, const_cast<__half*>(V), dims, strides, box,
             estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
             CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+static bool encode_v_map(CUtensorMap* map, const __half* V, int C, long long BP, int cgn) {
+  return cached_tensor_map(map, V, C, BP, cgn, 1, [&](CUtensorMap* m) {
+    return encode_v_map_raw(m, V, C, BP, cgn);
+  });
 }
 
 template <int TPC, int G>
@@ -1021,7 +1041,7 @@ const void* ot_ytma_fn() { return (const void*)output_transform_fast<4, 1, true,
 
 // y as [B][K][H_out][W_out] (W fastest), box {24, 6, 64, 1}: one TMA store per
 // 4-tile chunk.  Needs W_out % 8 == 0 (16-byte row stride).
-static bool encode_y_map(CUtensorMap* map, const __half* y, int B, int K, int H_out, int W_out) {
+static bool encode_y_map_raw(CUtensorMap* map, const __half* y, int B, int K, int H_out, int W_out) {
   EncodeTiledFn fn = encode_fn();
   if (!fn || (W_out % 8) || (reinterpret_cast<uintptr_t>(y) & 15)) return false;
   cuuint64_t dims[4] = {(cuuint64_t)W_out, (cuuint64_t)H_out, (cuuint64_t)K, (cuuint64_t)B};
@@ -1032,6 +1052,12 @@ static bool encode_y_map(CUtensorMap* map, const __half* y, int B, int K, int H_
   return fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4, const_cast<__half*>(y), dims, strides, box,
             estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
             CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+static bool encode_y_map(CUtensorMap* map, const __half* y, int B, int K, int H_out, int W_out) {
+  return cached_tensor_map(map, y, ((long long)B << 32) | (unsigned)K, ((long long)H_out << 32) | (unsigned)W_out, 0, 5, [&](CUtensorMap* m) {
+    return encode_y_map_raw(m, y, B, K, H_out, W_out);
+  });
 }
 
 // The TMA y-store output transform, on unless NOVA_OT_YTMA=0.
