@@ -8,12 +8,15 @@
 //
 // * Persistent kernel, one CTA per SM, tiles enumerated pos-major, then bp tile,
 //   then k tile, so CTAs running at the same time share U[pos] and V tiles in L2.
-// * Tile = 128 bp rows (MMA M, TMEM lanes) x BN output channels (MMA N <= 256)
-//   x 64 input channels per pipeline stage (one 128-byte SWIZZLE_128B row).
+// * Tile = 128 bp rows (MMA M, TMEM lanes) x BN output channels (MMA N <= 256;
+//   half of BN when BN-wide tiles would leave most SMs idle) x 64 input
+//   channels per pipeline stage (one 128-byte SWIZZLE_128B row).
 // * Warp 0: TMA producer (cp.async.bulk.tensor.3d, no multicast).  Warp 1: TMEM
-//   allocation and the single-thread tcgen05.mma issuer.  Warps 2-5: epilogue
-//   (tcgen05.ld -> FP16 -> global).  The accumulator is double buffered in TMEM
-//   (2 x BN columns) so the epilogue of tile i overlaps the MMAs of tile i+1.
+//   allocation and the single-thread tcgen05.mma issuer.  Warps 2-9: two
+//   epilogue warpgroups, one per accumulator buffer (tcgen05.ld -> FP16 ->
+//   32-row x 64-column swizzled smem slabs -> TMA tile stores of M).  The
+//   accumulator is double buffered in TMEM (2 x BN columns) so the epilogue of
+//   tile i overlaps the MMAs of tile i+1.
 // * Every mbarrier wait is bounded (globaltimer); on expiry the kernel records a
 //   status code in device memory, stops issuing work and returns.
 #include <algorithm>

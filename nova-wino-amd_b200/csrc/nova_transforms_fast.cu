@@ -8,16 +8,19 @@
 // lane = one full 128-byte line.
 //
 // Input transform:  image rows staged in shared memory, then V = B^T d B in
-//   registers.  With W % 8 == 0 (mode 1) the rows arrive by one TMA tile load,
-//   are transposed with ldmatrix.trans into [col][channel][row], and the V
-//   tiles go back out through shared memory by TMA tile stores; otherwise the
-//   staging is [row][col][channel] (66-half cell pitch = 33 words, odd:
-//   conflict-free) and V is written straight to V[pos][bp][c].
+//   registers.  With W % 8 == 0 (mode 1) the rows arrive by one TMA tile load
+//   and are transposed with ldmatrix.trans into [col][channel][row]; with
+//   W % 4 == 0 and even H (mode 2) they arrive as pair rows and are repacked
+//   into [row][col][channel] (66-half cell pitch = 33 words, odd:
+//   conflict-free).  In both TMA modes the V tiles go back out through shared
+//   memory by TMA tile stores; otherwise (mode 0) the rows are staged with
+//   plain loads and V is written straight to V[pos][bp][c].
 // Output transform: the block's M tiles arrive by TMA tile loads (or 64
 //   independent loads per lane when M cannot be described by a tensor map),
-//   Y = A M A^T in registers, parked in shared memory [row][col][k], then
-//   written as whole output row segments along w (warp per row, lane per
-//   column).
+//   Y = A M A^T in registers, parked in shared memory as [pixel][k].  With
+//   W_out % 8 == 0 the tile rows are transposed into a dense [k][row][col] box
+//   and leave by one TMA tile store; otherwise they are written as whole output
+//   row segments along w (warp per channel, lane per column).
 // Reference: input_transform_kernel(_mt) and output_transform_kernel(_mt),
 // Jayluci4/nova-wino-amd csrc/nova_winograd.hip:141-205, 264-328, 338-450.
 #include <algorithm>
