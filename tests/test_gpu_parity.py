@@ -93,6 +93,7 @@ PARITY_CASES = [
     (1, 3, 64, 50, 50, 1),       # C = 3: SIMT GEMM path
     (2, 16, 4, 12, 12, 1),       # K = 4: SIMT GEMM path
     (1, 8, 16, 1, 1, 1),         # single pixel
+    (3, 96, 80, 40, 40, 1),      # TMA paths with a partial last 64-channel group (x, V, y clipped)
 ]
 
 
