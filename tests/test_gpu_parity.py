@@ -94,6 +94,10 @@ PARITY_CASES = [
     (2, 16, 4, 12, 12, 1),       # K = 4: SIMT GEMM path
     (1, 8, 16, 1, 1, 1),         # single pixel
     (3, 96, 80, 40, 40, 1),      # TMA paths with a partial last 64-channel group (x, V, y clipped)
+    # SD 1.5 / SDXL UNet channel counts (configs 4 and 5) at small spatial sizes:
+    (1, 320, 320, 32, 32, 1),    # GEMM N = 160 (non-TMA epilogue)
+    (1, 640, 640, 16, 16, 1),    # N = 160, 4 column tiles
+    (1, 1280, 1280, 8, 8, 1),    # N = 256, 5 column tiles
 ]
 
 
