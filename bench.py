@@ -37,6 +37,14 @@ LAYERS = [  # (name, C = K, H = W)
     ("conv4_x", 256, 14),
     ("conv5_x", 512, 7),
 ]
+# SD 1.5 UNet 3x3 stride-1 shapes at a 64x64 latent (configs 4 and 5 use these
+# channel counts): per-layer timing only, the UNet model itself is not built.
+UNET_LAYERS = [
+    ("sd_320_64", 320, 64),
+    ("sd_640_32", 640, 32),
+    ("sd_1280_16", 1280, 16),
+    ("sd_1280_8", 1280, 8),
+]
 METRIC = "F(6,3) conv eff. TFLOP/s (direct-conv FLOPs / time), ResNet-50 3x3 s1 layer sweep"
 UNIT = "TFLOP/s"
 L2_BYTES = 126 * 1024 * 1024
@@ -232,12 +240,12 @@ def max_over_ranks(dist, value):
     return float(t.item())
 
 
-def build_layers(batch, device):
+def build_layers(batch, device, shapes=None):
     import numpy as np
     import torch
     from nova_winograd import NovaWinogradConv2d
     layers = []
-    for name, C, H in LAYERS:
+    for name, C, H in (shapes or LAYERS):
         rng = np.random.default_rng(1234 + C)
         x = torch.from_numpy(rng.standard_normal((batch, C, H, H), dtype=np.float32)).to(
             device=device, dtype=torch.float16)
@@ -549,6 +557,50 @@ def run_nova(args):
         dist.destroy_process_group()
 
 
+def run_unet_layers(args):
+    """SD 1.5 UNet 3x3 stride-1 layer shapes (UNET_LAYERS) at --batch: one step
+    is one forward of each, L2 flushed between steps, with the same layers
+    through torch's FP16 conv2d (cuDNN) for context.  Synthetic N(0,1) inputs and
+    Kaiming-normal weights; one GPU."""
+    import torch
+    device = torch.device("cuda", 0)
+    torch.cuda.set_device(device)
+    layers = build_layers(args.batch, device, UNET_LAYERS)
+    flush = make_flush(device)
+    flops_step = sum(direct_flops(args.batch, C, C, H) for _, C, H in UNET_LAYERS)
+
+    def step():
+        for _, _, _, conv, x in layers:
+            conv(x)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    evs = []
+    for _ in range(args.steps):
+        flush()
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        step()
+        e.record()
+        evs.append((s, e))
+    torch.cuda.synchronize()
+    total_ms = sum(s.elapsed_time(e) for s, e in evs)
+    emit({
+        "metric": "F(6,3) conv eff. TFLOP/s (direct-conv FLOPs / time), SD 1.5 UNet 3x3 s1 shapes",
+        "value": flops_step * args.steps / (total_ms / 1e3) / 1e12, "unit": "TFLOP/s",
+        "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": total_ms / args.steps, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f16",
+        "data": "synthetic (seeded N(0,1) FP16 inputs, Kaiming-normal FP32 weights)",
+        "config": {"workload": "sd15_unet_3x3_shapes", "layers": [l[0] for l in UNET_LAYERS],
+                   "batch_per_gpu": args.batch,
+                   "l2": "flushed between steps (write then read 2x L2)"},
+        "per_layer_vs_cudnn": vendor_layer_times(layers, flush),
+        "library": __import__("nova_winograd").ops.get_lib().nova_version().decode(),
+    })
+
+
 def run_resnet50(args):
     """torchvision ResNet-50 (random init, BN in eval mode
     with running mean 0 / var 1), FP16, 3x224x224 N(0,1) input; the 13 eligible
@@ -685,9 +737,10 @@ def main():
     ap.add_argument("--cpu-batch", type=int, default=1)
     ap.add_argument("--impl", choices=["nova", "reference"], default="nova")
     ap.add_argument("--no-cpu", action="store_true")
-    ap.add_argument("--workload", choices=["sweep", "resnet50"], default="sweep",
+    ap.add_argument("--workload", choices=["sweep", "resnet50", "unet"], default="sweep",
                     help="sweep: ResNet-50 3x3 layer sweep (BASELINE config 2, default); "
-                         "resnet50: whole model images/s (config 3)")
+                         "resnet50: whole model images/s (config 3); unet: SD 1.5 UNet 3x3 "
+                         "layer shapes (configs 4 and 5, per layer)")
     ap.add_argument("--fused", action="store_true",
                     help="with --profile-stages: run the fused single kernel instead (C, K <= 64)")
     ap.add_argument("--profile-stages", metavar="LAYER", default=None,
@@ -702,6 +755,9 @@ def main():
     elif args.workload == "resnet50":
         args.warmup = max(3, args.warmup)
         run_resnet50(args)
+    elif args.workload == "unet":
+        args.warmup = max(3, args.warmup)
+        run_unet_layers(args)
     else:
         args.warmup = max(3, args.warmup)
         run_nova(args)
