@@ -45,6 +45,12 @@ UNET_LAYERS = [
     ("sd_1280_16", 1280, 16),
     ("sd_1280_8", 1280, 8),
 ]
+# SDXL UNet 3x3 stride-1 shapes at a 128x128 latent (config 5).
+SDXL_LAYERS = [
+    ("sdxl_320_128", 320, 128),
+    ("sdxl_640_64", 640, 64),
+    ("sdxl_1280_32", 1280, 32),
+]
 METRIC = "F(6,3) conv eff. TFLOP/s (direct-conv FLOPs / time), ResNet-50 3x3 s1 layer sweep"
 UNIT = "TFLOP/s"
 L2_BYTES = 126 * 1024 * 1024
@@ -558,16 +564,18 @@ def run_nova(args):
 
 
 def run_unet_layers(args):
-    """SD 1.5 UNet 3x3 stride-1 layer shapes (UNET_LAYERS) at --batch: one step
-    is one forward of each, L2 flushed between steps, with the same layers
-    through torch's FP16 conv2d (cuDNN) for context.  Synthetic N(0,1) inputs and
-    Kaiming-normal weights; one GPU."""
+    """UNet 3x3 stride-1 layer shapes (UNET_LAYERS for SD 1.5, SDXL_LAYERS for
+    SDXL) at --batch: one step is one forward of each, L2 flushed between steps,
+    with the same layers through torch's FP16 conv2d (cuDNN) for context.
+    Synthetic N(0,1) inputs and Kaiming-normal weights; one GPU."""
     import torch
+    shapes = SDXL_LAYERS if args.workload == "sdxl" else UNET_LAYERS
+    model = "SDXL" if args.workload == "sdxl" else "SD 1.5"
     device = torch.device("cuda", 0)
     torch.cuda.set_device(device)
-    layers = build_layers(args.batch, device, UNET_LAYERS)
+    layers = build_layers(args.batch, device, shapes)
     flush = make_flush(device)
-    flops_step = sum(direct_flops(args.batch, C, C, H) for _, C, H in UNET_LAYERS)
+    flops_step = sum(direct_flops(args.batch, C, C, H) for _, C, H in shapes)
 
     def step():
         for _, _, _, conv, x in layers:
@@ -587,13 +595,13 @@ def run_unet_layers(args):
     torch.cuda.synchronize()
     total_ms = sum(s.elapsed_time(e) for s, e in evs)
     emit({
-        "metric": "F(6,3) conv eff. TFLOP/s (direct-conv FLOPs / time), SD 1.5 UNet 3x3 s1 shapes",
+        "metric": f"F(6,3) conv eff. TFLOP/s (direct-conv FLOPs / time), {model} UNet 3x3 s1 shapes",
         "value": flops_step * args.steps / (total_ms / 1e3) / 1e12, "unit": "TFLOP/s",
         "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": total_ms / args.steps, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "f16",
         "data": "synthetic (seeded N(0,1) FP16 inputs, Kaiming-normal FP32 weights)",
-        "config": {"workload": "sd15_unet_3x3_shapes", "layers": [l[0] for l in UNET_LAYERS],
+        "config": {"workload": f"{args.workload}_unet_3x3_shapes", "layers": [l[0] for l in shapes],
                    "batch_per_gpu": args.batch,
                    "l2": "flushed between steps (write then read 2x L2)"},
         "per_layer_vs_cudnn": vendor_layer_times(layers, flush),
@@ -737,10 +745,11 @@ def main():
     ap.add_argument("--cpu-batch", type=int, default=1)
     ap.add_argument("--impl", choices=["nova", "reference"], default="nova")
     ap.add_argument("--no-cpu", action="store_true")
-    ap.add_argument("--workload", choices=["sweep", "resnet50", "unet"], default="sweep",
+    ap.add_argument("--workload", choices=["sweep", "resnet50", "unet", "sdxl"], default="sweep",
                     help="sweep: ResNet-50 3x3 layer sweep (BASELINE config 2, default); "
                          "resnet50: whole model images/s (config 3); unet: SD 1.5 UNet 3x3 "
-                         "layer shapes (configs 4 and 5, per layer)")
+                         "layer shapes (config 4, per layer); sdxl: SDXL UNet 3x3 layer "
+                         "shapes (config 5, per layer)")
     ap.add_argument("--fused", action="store_true",
                     help="with --profile-stages: run the fused single kernel instead (C, K <= 64)")
     ap.add_argument("--profile-stages", metavar="LAYER", default=None,
@@ -755,7 +764,7 @@ def main():
     elif args.workload == "resnet50":
         args.warmup = max(3, args.warmup)
         run_resnet50(args)
-    elif args.workload == "unet":
+    elif args.workload in ("unet", "sdxl"):
         args.warmup = max(3, args.warmup)
         run_unet_layers(args)
     else:
