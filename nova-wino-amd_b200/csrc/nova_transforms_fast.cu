@@ -610,11 +610,29 @@ struct PlaneGeo {
 
 // Plane args: BP/row window semantics as Args; row0 and lrow0 are tile rows and
 // are multiples of nh here (blocks own whole images).
-template <int TR, int TC, int kW>
+// Untiled bulk copy global -> shared, completing on an mbarrier (no multicast):
+// both addresses 16-byte aligned, bytes a multiple of 16.
+__device__ __forceinline__ void bulk_load(uint32_t dst, const void* src, uint32_t bytes,
+                                          uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+          dst),
+      "l"(src), "r"(bytes), "r"(bar)
+      : "memory");
+}
+
+// kLand = 0: each warp loads channels cell by cell with 2-byte loads, two
+// channels per round (one memory round trip per round).  kLand = 32 or 64: the
+// block's channels of one image are one contiguous span of x ([c][h][w]); it
+// lands in shared memory by bulk copies of kLand channels (one round trip
+// each) while the zero border of the padded plane is written, and is then
+// transposed into [cell][channel].  Needs C % 8 == 0 and a 16-byte aligned x.
+template <int TR, int TC, int kW, int kLand>
 __global__ void __launch_bounds__(32 * PlaneGeo<TR, TC, kW>::kWarps, PlaneGeo<TR, TC, kW>::kMinBlocks)
     input_transform_plane(const __half* __restrict__ x, __half* __restrict__ V, const Args a) {
   using Pg = PlaneGeo<TR, TC, kW>;
-  extern __shared__ __align__(16) __half xs[];  // [kCells][kPitch]
+  extern __shared__ __align__(16) __half xs[];  // [kCells][kPitch], then the landing
+  __shared__ __align__(8) uint64_t land_bar;
   const int cg = blockIdx.x;
   const long long limg = a.lrow0 / TR + blockIdx.y;  // image inside the window
   const long long b = a.row0 / TR + limg;
@@ -623,39 +641,95 @@ __global__ void __launch_bounds__(32 * PlaneGeo<TR, TC, kW>::kWarps, PlaneGeo<TR
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   pdl_wait();
 
-  // Lane's padded-plane cells: global offset inside the image plane (or -1 for
-  // zero padding) and shared-memory cell offset.
-  int goff[Pg::kInPerLane], soff[Pg::kInPerLane];
-#pragma unroll
-  for (int m = 0; m < Pg::kInPerLane; ++m) {
-    const int e = lane + 32 * m;
-    const int r = e / Pg::kCols, col = e - (e / Pg::kCols) * Pg::kCols;
-    const int h = r - pad, w = col - pad;
-    soff[m] = e < Pg::kCells ? e * Pg::kPitch : -1;
-    goff[m] = (e < Pg::kCells && h >= 0 && h < H && w >= 0 && w < W) ? h * W + w : -1;
-  }
   const long long plane_x = (long long)H * W;
   const __half* xb = x + (b * C + c0) * plane_x;
-  // Two channels per round: their loads are all in flight before any store.
-  constexpr int kCh = 2;
-  for (int cl0 = warp; cl0 < 64; cl0 += Pg::kWarps * kCh) {
-    __half v[kCh][Pg::kInPerLane];
-#pragma unroll
-    for (int u = 0; u < kCh; ++u) {
-      const int cl = cl0 + u * Pg::kWarps;
-      const bool cok = cl < 64 && c0 + cl < C;
-      const __half* cp = xb + (cok ? cl : 0) * plane_x;
-#pragma unroll
-      for (int m = 0; m < Pg::kInPerLane; ++m)
-        v[u][m] = (cok && goff[m] >= 0) ? cp[goff[m]] : __ushort_as_half(0);
+  if constexpr (kLand > 0) {
+    const int HW = H * W;
+    const int nch = C - c0 < 64 ? C - c0 : 64;
+    __half* land = xs + Pg::kCells * Pg::kPitch;  // [kLand][H*W]
+    const uint32_t land_s = static_cast<uint32_t>(__cvta_generic_to_shared(land));
+    const uint32_t bar = static_cast<uint32_t>(__cvta_generic_to_shared(&land_bar));
+    if (threadIdx.x == 0) {
+      asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(bar) : "memory");
+      asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
+    __syncthreads();
+    // Padded cell of each of the lane's image cells e = lane + 32 m.
+    int cellofs[Pg::kInPerLane];
 #pragma unroll
-    for (int u = 0; u < kCh; ++u) {
-      const int cl = cl0 + u * Pg::kWarps;
-      if (cl < 64) {
+    for (int m = 0; m < Pg::kInPerLane; ++m) {
+      const int e = lane + 32 * m;
+      const int h = e / W, w = e - (e / W) * W;
+      cellofs[m] = e < HW ? ((h + pad) * Pg::kCols + w + pad) * Pg::kPitch : -1;
+    }
+    uint32_t phase = 0;
+    for (int ch0 = 0; ch0 < nch; ch0 += kLand) {
+      const int n = nch - ch0 < kLand ? nch - ch0 : kLand;
+      if (threadIdx.x == 0) {
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar),
+                     "r"((uint32_t)(n * HW * 2))
+                     : "memory");
+        bulk_load(land_s, xb + (long long)ch0 * HW, (uint32_t)(n * HW * 2), bar);
+      }
+      if (ch0 == 0) {
+        // Zero border cells (channel words 0..31) while the copy is in flight.
+        uint32_t* xw = reinterpret_cast<uint32_t*>(xs);
+        for (int cell = warp; cell < Pg::kCells; cell += Pg::kWarps) {
+          const int r = cell / Pg::kCols, col = cell - (cell / Pg::kCols) * Pg::kCols;
+          const int h = r - pad, w = col - pad;
+          if (h < 0 || h >= H || w < 0 || w >= W) xw[cell * (Pg::kPitch / 2) + lane] = 0u;
+        }
+      }
+      if (!mbar_wait_bounded(bar, phase)) return;
+      phase ^= 1u;
+      // Channel pairs: lanes walk cells (consecutive halves of one channel).
+      for (int p2 = warp; 2 * p2 < n; p2 += Pg::kWarps) {
+        const __half* s0 = land + (2 * p2) * HW;
+        const __half* s1 = s0 + HW;
 #pragma unroll
+        for (int m = 0; m < Pg::kInPerLane; ++m) {
+          const int e = lane + 32 * m;
+          if (cellofs[m] >= 0)
+            *reinterpret_cast<__half2*>(xs + cellofs[m] + ch0 + 2 * p2) =
+                __halves2half2(s0[e], s1[e]);
+        }
+      }
+      __syncthreads();  // the landing is read before it is refilled
+    }
+  } else {
+    // Lane's padded-plane cells: global offset inside the image plane (or -1 for
+    // zero padding) and shared-memory cell offset.
+    int goff[Pg::kInPerLane], soff[Pg::kInPerLane];
+  #pragma unroll
+    for (int m = 0; m < Pg::kInPerLane; ++m) {
+      const int e = lane + 32 * m;
+      const int r = e / Pg::kCols, col = e - (e / Pg::kCols) * Pg::kCols;
+      const int h = r - pad, w = col - pad;
+      soff[m] = e < Pg::kCells ? e * Pg::kPitch : -1;
+      goff[m] = (e < Pg::kCells && h >= 0 && h < H && w >= 0 && w < W) ? h * W + w : -1;
+    }
+    // Two channels per round: their loads are all in flight before any store.
+    constexpr int kCh = 2;
+    for (int cl0 = warp; cl0 < 64; cl0 += Pg::kWarps * kCh) {
+      __half v[kCh][Pg::kInPerLane];
+  #pragma unroll
+      for (int u = 0; u < kCh; ++u) {
+        const int cl = cl0 + u * Pg::kWarps;
+        const bool cok = cl < 64 && c0 + cl < C;
+        const __half* cp = xb + (cok ? cl : 0) * plane_x;
+  #pragma unroll
         for (int m = 0; m < Pg::kInPerLane; ++m)
-          if (soff[m] >= 0) xs[soff[m] + cl] = v[u][m];
+          v[u][m] = (cok && goff[m] >= 0) ? cp[goff[m]] : __ushort_as_half(0);
+      }
+  #pragma unroll
+      for (int u = 0; u < kCh; ++u) {
+        const int cl = cl0 + u * Pg::kWarps;
+        if (cl < 64) {
+  #pragma unroll
+          for (int m = 0; m < Pg::kInPerLane; ++m)
+            if (soff[m] >= 0) xs[soff[m] + cl] = v[u][m];
+        }
       }
     }
   }
@@ -796,8 +870,8 @@ __global__ void __launch_bounds__(32 * PlaneGeo<TR, TC, kW>::kWarps, PlaneGeo<TR
 }
 
 // Kernel addresses for the shared-memory opt-in.
-template <int TR, int TC, int kW>
-const void* it_plane_fn() { return (const void*)input_transform_plane<TR, TC, kW>; }
+template <int TR, int TC, int kW, int kLand>
+const void* it_plane_fn() { return (const void*)input_transform_plane<TR, TC, kW, kLand>; }
 template <int TR, int TC, int kW, bool kTma>
 const void* ot_plane_fn() { return (const void*)output_transform_plane<TR, TC, kW, kTma>; }
 
@@ -811,17 +885,50 @@ static bool plane_small(long long blocks) {
   return blocks < sms[dev];
 }
 
-template <int TR, int TC, int kW>
-static void launch_it_plane_w(const __half* x, __half* V, Args a, long long nimg, unsigned gx,
+// Bulk-landed plane input (kLand channels per copy) for the throughput shapes
+// of fewer than 9 tiles: 7x7 images, 512 channels, batch 128 went from 27.0 to
+// 21.5 us.  At 3x3 tiles the landing buffer costs a block per SM and the
+// kernel is issue-bound, so the per-lane loader stays (31.7 us against 32.7
+// with 32-channel copies and 32.8 with 64, 14x14 images, 256 channels).
+// NOVA_PLANE_LAND=0, 32 or 64 forces a choice.
+static int plane_land_choice(int TRTC) {
+  static const int env = [] {
+    const char* e = std::getenv("NOVA_PLANE_LAND");
+    return e ? std::atoi(e) : -1;
+  }();
+  if (env == 0 || env == 32 || env == 64) return env;
+  return TRTC >= 9 ? 0 : 64;
+}
+
+template <int TR, int TC, int kW, int kLand>
+static void launch_it_plane_k(const __half* x, __half* V, Args a, long long nimg, unsigned gx,
                               cudaStream_t s) {
   using Pg = PlaneGeo<TR, TC, kW>;
-  if (!smem_optin_once<it_plane_fn<TR, TC, kW>>(Pg::kInSmem)) return;
+  const size_t smem = Pg::kInSmem + (size_t)kLand * a.H * a.W * 2;
+  if (!smem_optin_once<it_plane_fn<TR, TC, kW, kLand>>(Pg::kInSmem +
+                                                         (size_t)kLand * Pg::kCells * 2))
+    return;
   for (long long done = 0; done < nimg; done += kMaxGridY) {
     a.lrow0 = done * TR;
     dim3 grid(gx, (unsigned)std::min(kMaxGridY, nimg - done));
-    launch_pdl(kPdlInput, input_transform_plane<TR, TC, kW>, grid, dim3(32 * Pg::kWarps),
-               Pg::kInSmem, s, x, V, a);
+    launch_pdl(kPdlInput, input_transform_plane<TR, TC, kW, kLand>, grid, dim3(32 * Pg::kWarps),
+               smem, s, x, V, a);
   }
+}
+
+template <int TR, int TC, int kW>
+static void launch_it_plane_w(const __half* x, __half* V, Args a, long long nimg, unsigned gx,
+                              cudaStream_t s) {
+  constexpr bool kThroughput = kW != (TR * TC < 2 ? 2 : TR * TC);
+  const int land = (kThroughput && a.C % 8 == 0 && (reinterpret_cast<uintptr_t>(x) & 15) == 0)
+                       ? plane_land_choice(TR * TC)
+                       : 0;
+  if (land == 64)
+    launch_it_plane_k<TR, TC, kW, 64>(x, V, a, nimg, gx, s);
+  else if (land == 32)
+    launch_it_plane_k<TR, TC, kW, 32>(x, V, a, nimg, gx, s);
+  else
+    launch_it_plane_k<TR, TC, kW, 0>(x, V, a, nimg, gx, s);
 }
 
 template <int TR, int TC>

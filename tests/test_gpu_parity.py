@@ -202,15 +202,12 @@ def test_plane_launch_shapes_agree():
     check_parity(x[:2], w, 1, yb[:2])
 
 
-def test_programmatic_launch_off_matches_default():
-    # The same forward in a child process with programmatic dependent launch
-    # disabled (NOVA_PDL_MASK=0) writes the same bytes.
+def forward_in_child(x, w, pad, env_overrides):
+    """The same C-ABI forward in a child process with extra environment switches."""
     import os
     import subprocess
     import sys
     import tempfile
-    x, w = o.synthetic_case(3, 64, 128, 30, 30, seed=505)
-    y, _ = run_forward(x, w, 1)
     here = os.path.dirname(os.path.abspath(__file__))
     root = os.path.dirname(here)
     with tempfile.TemporaryDirectory() as tmp:
@@ -222,12 +219,50 @@ def test_programmatic_launch_off_matches_default():
             f"{os.path.join(root, 'oracle')!r}]\n"
             "from test_gpu_parity import run_forward\n"
             f"x = np.load({os.path.join(tmp, 'x.npy')!r}); w = np.load({os.path.join(tmp, 'w.npy')!r})\n"
-            "y, _ = run_forward(x, w, 1)\n"
+            f"y, _ = run_forward(x, w, {pad})\n"
             f"np.save({os.path.join(tmp, 'y.npy')!r}, y)\n")
-        env = dict(os.environ, NOVA_PDL_MASK="0")
+        env = dict(os.environ, **env_overrides)
         subprocess.run([sys.executable, "-c", code], check=True, env=env, timeout=600)
-        y0 = np.load(os.path.join(tmp, "y.npy"))
-    np.testing.assert_array_equal(y, y0)
+        return np.load(os.path.join(tmp, "y.npy"))
+
+
+def test_programmatic_launch_off_matches_default():
+    # The same forward in a child process with programmatic dependent launch
+    # disabled (NOVA_PDL_MASK=0) writes the same bytes.
+    x, w = o.synthetic_case(3, 64, 128, 30, 30, seed=505)
+    y, _ = run_forward(x, w, 1)
+    np.testing.assert_array_equal(y, forward_in_child(x, w, 1, {"NOVA_PDL_MASK": "0"}))
+
+
+# Plane-mode shapes (images of at most 3x3 tiles) at batches that launch at
+# least one block per SM, so the throughput plane kernels run: images of
+# fewer than 9 tiles land by bulk copies of 64 channels.
+PLANE_THROUGHPUT_CASES = [
+    (80, 72, 64, 14, 14, 1),     # 3x3 tiles, last 64-channel group holds 8 channels
+    (40, 264, 72, 7, 7, 1),      # 2x2 tiles, odd H*W, last C and K groups hold 8 channels
+    (160, 64, 32, 12, 12, 0),    # pad 0: 10x10 output, 2x2 tiles
+    (150, 16, 16, 4, 4, 1),      # 1x1 tile, 16 channels
+]
+
+
+@pytest.mark.parametrize("B,C,K,H,W,pad", PLANE_THROUGHPUT_CASES)
+def test_plane_throughput_parity(B, C, K, H, W, pad):
+    x, w = o.synthetic_case(B, C, K, H, W, seed=606 + B + C + H)
+    y, _ = run_forward(x, w, pad)
+    check_parity(x[:4], w, pad, y[:4])
+    check_parity(x[-4:], w, pad, y[-4:])
+
+
+def test_plane_bulk_input_matches_lane_loads():
+    # The bulk-landed plane input stages the same values as the per-lane
+    # loader (NOVA_PLANE_LAND=0): the outputs are bit-identical.
+    # 3x3 tiles compare forced 32-channel copies with the default loader.
+    for (B, C, K, H, W, pad), env in ((PLANE_THROUGHPUT_CASES[0], {"NOVA_PLANE_LAND": "32"}),
+                                      (PLANE_THROUGHPUT_CASES[1], {"NOVA_PLANE_LAND": "0"}),
+                                      (PLANE_THROUGHPUT_CASES[2], {"NOVA_PLANE_LAND": "0"})):
+        x, w = o.synthetic_case(B, C, K, H, W, seed=707 + C)
+        y, _ = run_forward(x, w, pad)
+        np.testing.assert_array_equal(y, forward_in_child(x, w, pad, env))
 
 
 def test_empty_batch_is_a_no_op():
