@@ -622,7 +622,8 @@ __device__ __forceinline__ void bulk_load(uint32_t dst, const void* src, uint32_
 }
 
 // kLand = 0: each warp loads channels cell by cell with 2-byte loads, two
-// channels per round (one memory round trip per round).  kLand = 32 or 64: the
+// channels per round (one memory round trip per round).  kLand = 2 (W even):
+// 4-byte loads of cell pairs, four channels per round.  kLand = 32 or 64: the
 // block's channels of one image are one contiguous span of x ([c][h][w]); it
 // lands in shared memory by bulk copies of kLand channels (one round trip
 // each) while the zero border of the padded plane is written, and is then
@@ -643,7 +644,7 @@ __global__ void __launch_bounds__(32 * PlaneGeo<TR, TC, kW>::kWarps, PlaneGeo<TR
 
   const long long plane_x = (long long)H * W;
   const __half* xb = x + (b * C + c0) * plane_x;
-  if constexpr (kLand > 0) {
+  if constexpr (kLand >= 32) {
     const int HW = H * W;
     const int nch = C - c0 < 64 ? C - c0 : 64;
     __half* land = xs + Pg::kCells * Pg::kPitch;  // [kLand][H*W]
@@ -697,11 +698,57 @@ __global__ void __launch_bounds__(32 * PlaneGeo<TR, TC, kW>::kWarps, PlaneGeo<TR
       }
       __syncthreads();  // the landing is read before it is refilled
     }
+  } else if constexpr (kLand == 2) {
+    // W even: one 4-byte load brings cells (w, w + 1) of a row of one
+    // channel, so a channel takes H*W/64 loads per lane and four channels fit
+    // a round.  The zero border is written once, not loaded.
+    const int HW2 = (H * W) >> 1;
+    constexpr int kPairPer = (Pg::kCells / 2 + 31) / 32;
+    int pofs[kPairPer];  // padded cell of the pair's first element, -1 past the plane
+#pragma unroll
+    for (int m = 0; m < kPairPer; ++m) {
+      const int e = 2 * (lane + 32 * m);
+      const int h = e / W, w = e - (e / W) * W;
+      pofs[m] = e < 2 * HW2 ? ((h + pad) * Pg::kCols + w + pad) * Pg::kPitch : -1;
+    }
+    uint32_t* xw = reinterpret_cast<uint32_t*>(xs);
+    for (int cell = warp; cell < Pg::kCells; cell += Pg::kWarps) {
+      const int r = cell / Pg::kCols, col = cell - (cell / Pg::kCols) * Pg::kCols;
+      const int h = r - pad, w = col - pad;
+      if (h < 0 || h >= H || w < 0 || w >= W) xw[cell * (Pg::kPitch / 2) + lane] = 0u;
+    }
+    const uint32_t* xb2 = reinterpret_cast<const uint32_t*>(xb);
+    constexpr int kCh = 4;
+    for (int cl0 = warp; cl0 < 64; cl0 += Pg::kWarps * kCh) {
+      uint32_t v[kCh][kPairPer];
+#pragma unroll
+      for (int u = 0; u < kCh; ++u) {
+        const int cl = cl0 + u * Pg::kWarps;
+        const bool cok = cl < 64 && c0 + cl < C;
+        const uint32_t* cp = xb2 + (cok ? cl : 0) * (long long)HW2;
+#pragma unroll
+        for (int m = 0; m < kPairPer; ++m)
+          v[u][m] = (cok && pofs[m] >= 0) ? __ldg(cp + lane + 32 * m) : 0u;
+      }
+#pragma unroll
+      for (int u = 0; u < kCh; ++u) {
+        const int cl = cl0 + u * Pg::kWarps;
+        if (cl < 64) {
+#pragma unroll
+          for (int m = 0; m < kPairPer; ++m) {
+            if (pofs[m] >= 0) {
+              xs[pofs[m] + cl] = __ushort_as_half((unsigned short)(v[u][m] & 0xffffu));
+              xs[pofs[m] + Pg::kPitch + cl] = __ushort_as_half((unsigned short)(v[u][m] >> 16));
+            }
+          }
+        }
+      }
+    }
   } else {
     // Lane's padded-plane cells: global offset inside the image plane (or -1 for
     // zero padding) and shared-memory cell offset.
     int goff[Pg::kInPerLane], soff[Pg::kInPerLane];
-  #pragma unroll
+#pragma unroll
     for (int m = 0; m < Pg::kInPerLane; ++m) {
       const int e = lane + 32 * m;
       const int r = e / Pg::kCols, col = e - (e / Pg::kCols) * Pg::kCols;
@@ -713,20 +760,20 @@ __global__ void __launch_bounds__(32 * PlaneGeo<TR, TC, kW>::kWarps, PlaneGeo<TR
     constexpr int kCh = 2;
     for (int cl0 = warp; cl0 < 64; cl0 += Pg::kWarps * kCh) {
       __half v[kCh][Pg::kInPerLane];
-  #pragma unroll
+#pragma unroll
       for (int u = 0; u < kCh; ++u) {
         const int cl = cl0 + u * Pg::kWarps;
         const bool cok = cl < 64 && c0 + cl < C;
         const __half* cp = xb + (cok ? cl : 0) * plane_x;
-  #pragma unroll
+#pragma unroll
         for (int m = 0; m < Pg::kInPerLane; ++m)
           v[u][m] = (cok && goff[m] >= 0) ? cp[goff[m]] : __ushort_as_half(0);
       }
-  #pragma unroll
+#pragma unroll
       for (int u = 0; u < kCh; ++u) {
         const int cl = cl0 + u * Pg::kWarps;
         if (cl < 64) {
-  #pragma unroll
+#pragma unroll
           for (int m = 0; m < Pg::kInPerLane; ++m)
             if (soff[m] >= 0) xs[soff[m] + cl] = v[u][m];
         }
@@ -888,25 +935,25 @@ static bool plane_small(long long blocks) {
 // Bulk-landed plane input (kLand channels per copy) for the throughput shapes
 // of fewer than 9 tiles: 7x7 images, 512 channels, batch 128 went from 27.0 to
 // 21.5 us.  At 3x3 tiles the landing buffer costs a block per SM and the
-// kernel is issue-bound, so the per-lane loader stays (31.7 us against 32.7
-// with 32-channel copies and 32.8 with 64, 14x14 images, 256 channels).
-// NOVA_PLANE_LAND=0, 32 or 64 forces a choice.
+// kernel is issue-bound (32.7 us with 32-channel copies, 32.8 with 64, 14x14
+// images, 256 channels); there cell-pair loads take it from 31.7 to 27.6 us.
+// NOVA_PLANE_LAND=0, 2 (cell-pair loads), 32 or 64 forces a choice.
 static int plane_land_choice(int TRTC) {
   static const int env = [] {
     const char* e = std::getenv("NOVA_PLANE_LAND");
     return e ? std::atoi(e) : -1;
   }();
-  if (env == 0 || env == 32 || env == 64) return env;
-  return TRTC >= 9 ? 0 : 64;
+  if (env == 0 || env == 2 || env == 32 || env == 64) return env;
+  return TRTC >= 9 ? 2 : 64;
 }
 
 template <int TR, int TC, int kW, int kLand>
 static void launch_it_plane_k(const __half* x, __half* V, Args a, long long nimg, unsigned gx,
                               cudaStream_t s) {
   using Pg = PlaneGeo<TR, TC, kW>;
-  const size_t smem = Pg::kInSmem + (size_t)kLand * a.H * a.W * 2;
-  if (!smem_optin_once<it_plane_fn<TR, TC, kW, kLand>>(Pg::kInSmem +
-                                                         (size_t)kLand * Pg::kCells * 2))
+  constexpr size_t kLandCh = kLand >= 32 ? kLand : 0;  // channels of the bulk landing buffer
+  const size_t smem = Pg::kInSmem + kLandCh * a.H * a.W * 2;
+  if (!smem_optin_once<it_plane_fn<TR, TC, kW, kLand>>(Pg::kInSmem + kLandCh * Pg::kCells * 2))
     return;
   for (long long done = 0; done < nimg; done += kMaxGridY) {
     a.lrow0 = done * TR;
@@ -920,13 +967,16 @@ template <int TR, int TC, int kW>
 static void launch_it_plane_w(const __half* x, __half* V, Args a, long long nimg, unsigned gx,
                               cudaStream_t s) {
   constexpr bool kThroughput = kW != (TR * TC < 2 ? 2 : TR * TC);
-  const int land = (kThroughput && a.C % 8 == 0 && (reinterpret_cast<uintptr_t>(x) & 15) == 0)
-                       ? plane_land_choice(TR * TC)
-                       : 0;
+  int land = (kThroughput && a.C % 8 == 0 && (reinterpret_cast<uintptr_t>(x) & 15) == 0)
+                 ? plane_land_choice(TR * TC)
+                 : 0;
+  if (land == 2 && (a.W % 2 || (reinterpret_cast<uintptr_t>(x) & 3))) land = 0;
   if (land == 64)
     launch_it_plane_k<TR, TC, kW, 64>(x, V, a, nimg, gx, s);
   else if (land == 32)
     launch_it_plane_k<TR, TC, kW, 32>(x, V, a, nimg, gx, s);
+  else if (land == 2)
+    launch_it_plane_k<TR, TC, kW, 2>(x, V, a, nimg, gx, s);
   else
     launch_it_plane_k<TR, TC, kW, 0>(x, V, a, nimg, gx, s);
 }

@@ -236,12 +236,15 @@ def test_programmatic_launch_off_matches_default():
 
 # Plane-mode shapes (images of at most 3x3 tiles) at batches that launch at
 # least one block per SM, so the throughput plane kernels run: images of
-# fewer than 9 tiles land by bulk copies of 64 channels.
+# fewer than 9 tiles land by bulk copies of 64 channels; 3x3-tile images with
+# even W load cell pairs with 4-byte loads, odd W keeps 2-byte loads.
 PLANE_THROUGHPUT_CASES = [
     (80, 72, 64, 14, 14, 1),     # 3x3 tiles, last 64-channel group holds 8 channels
     (40, 264, 72, 7, 7, 1),      # 2x2 tiles, odd H*W, last C and K groups hold 8 channels
     (160, 64, 32, 12, 12, 0),    # pad 0: 10x10 output, 2x2 tiles
     (150, 16, 16, 4, 4, 1),      # 1x1 tile, 16 channels
+    (160, 64, 32, 20, 20, 0),    # pad 0, 3x3 tiles over a full 20x20 input plane
+    (150, 64, 64, 15, 15, 1),    # 3x3 tiles, odd W
 ]
 
 
@@ -253,13 +256,17 @@ def test_plane_throughput_parity(B, C, K, H, W, pad):
     check_parity(x[-4:], w, pad, y[-4:])
 
 
-def test_plane_bulk_input_matches_lane_loads():
-    # The bulk-landed plane input stages the same values as the per-lane
-    # loader (NOVA_PLANE_LAND=0): the outputs are bit-identical.
-    # 3x3 tiles compare forced 32-channel copies with the default loader.
-    for (B, C, K, H, W, pad), env in ((PLANE_THROUGHPUT_CASES[0], {"NOVA_PLANE_LAND": "32"}),
-                                      (PLANE_THROUGHPUT_CASES[1], {"NOVA_PLANE_LAND": "0"}),
-                                      (PLANE_THROUGHPUT_CASES[2], {"NOVA_PLANE_LAND": "0"})):
+def test_plane_input_loaders_agree():
+    # The plane input loaders stage the same values: the outputs are
+    # bit-identical.
+    # Every loader (0: 2-byte lane loads, 2: cell pairs, 32/64: bulk copies)
+    # against the default one for the shape.
+    cases = PLANE_THROUGHPUT_CASES
+    for (B, C, K, H, W, pad), env in ((cases[0], {"NOVA_PLANE_LAND": "0"}),
+                                      (cases[0], {"NOVA_PLANE_LAND": "32"}),
+                                      (cases[1], {"NOVA_PLANE_LAND": "0"}),
+                                      (cases[2], {"NOVA_PLANE_LAND": "2"}),
+                                      (cases[4], {"NOVA_PLANE_LAND": "0"})):
         x, w = o.synthetic_case(B, C, K, H, W, seed=707 + C)
         y, _ = run_forward(x, w, pad)
         np.testing.assert_array_equal(y, forward_in_child(x, w, pad, env))
