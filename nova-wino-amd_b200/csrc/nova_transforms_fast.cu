@@ -56,6 +56,9 @@ constexpr int kMaxTPC = 6;
 #ifndef NOVA_IT_MIN_BLOCKS
 #define NOVA_IT_MIN_BLOCKS 3  // 128 registers: 3 blocks of 5 warps per SM
 #endif
+#ifndef NOVA_PLANE_PAIR_CH
+#define NOVA_PLANE_PAIR_CH 6  // channels per round of the cell-pair plane loader (4: 28.6 us, 6: 26.7, 8: 26.6 at conv4_x batch 128)
+#endif
 #ifndef NOVA_OT_MIN_BLOCKS
 #define NOVA_OT_MIN_BLOCKS 3
 #endif
@@ -718,7 +721,7 @@ __global__ void __launch_bounds__(32 * PlaneGeo<TR, TC, kW>::kWarps, PlaneGeo<TR
       if (h < 0 || h >= H || w < 0 || w >= W) xw[cell * (Pg::kPitch / 2) + lane] = 0u;
     }
     const uint32_t* xb2 = reinterpret_cast<const uint32_t*>(xb);
-    constexpr int kCh = 4;
+    constexpr int kCh = NOVA_PLANE_PAIR_CH;
     for (int cl0 = warp; cl0 < 64; cl0 += Pg::kWarps * kCh) {
       uint32_t v[kCh][kPairPer];
 #pragma unroll
