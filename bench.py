@@ -569,8 +569,8 @@ def run_unet_layers(args):
     with the same layers through torch's FP16 conv2d (cuDNN) for context.
     Synthetic N(0,1) inputs and Kaiming-normal weights; one GPU."""
     import torch
-    shapes = SDXL_LAYERS if args.workload == "sdxl" else UNET_LAYERS
-    model = "SDXL" if args.workload == "sdxl" else "SD 1.5"
+    shapes = SDXL_LAYERS if args.workload == "sdxl_layers" else UNET_LAYERS
+    model = "SDXL" if args.workload == "sdxl_layers" else "SD 1.5"
     device = torch.device("cuda", 0)
     torch.cuda.set_device(device)
     layers = build_layers(args.batch, device, shapes)
@@ -684,6 +684,102 @@ def run_resnet50(args):
         dist.destroy_process_group()
 
 
+def run_unet_model(args):
+    """BASELINE configs 4 and 5: one denoising step of a random-init UNet
+    (unet_callers.SD15 on a 4x64x64 latent with a 77x768 context, or
+    unet_callers.SDXL on 4x128x128 with 77x2048, pooled text and time ids),
+    FP16, every eligible 3x3 stride-1 conv (49 / 38) replaced by
+    replace_conv2d_with_nova.  Data parallel by batch: every rank runs --batch
+    latents per step (weak scaling).  The same model without replacement
+    (cuDNN) is timed alongside and its output compared."""
+    import copy
+    import torch
+    import unet_callers as U
+    from nova_winograd import replace_conv2d_with_nova
+    world, rank, local, dist = setup_dist()
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    spec, latent, name = ((U.SD15, 64, "SD 1.5") if args.workload == "sd15"
+                          else (U.SDXL, 128, "SDXL"))
+    torch.manual_seed(1234)  # the same weights on every rank
+    with torch.device(device):
+        ref = U.UNet(spec)
+    ref = ref.half().eval()
+    model = copy.deepcopy(ref)
+    n_rep = replace_conv2d_with_nova(model, verbose=False)
+    x, t, ctx, extra = U.make_inputs(spec, args.batch, latent, device, seed=100 + rank)
+
+    def step(m, xs, ctxs, ex):
+        return m(xs, t, ctxs, **ex)
+
+    def timed(m):
+        with torch.no_grad():
+            for _ in range(args.warmup):
+                out = step(m, x, ctx, extra)
+            barrier(dist)
+            s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            s.record()
+            for _ in range(args.steps):
+                out = step(m, x, ctx, extra)
+            e.record()
+            torch.cuda.synchronize()
+        return max_over_ranks(dist, s.elapsed_time(e)), out
+
+    uuid = str(torch.cuda.get_device_properties(device).uuid)
+    sampler = ClockSampler(uuid if uuid.startswith("GPU-") else f"GPU-{uuid}")
+    sampler.start()
+    ms, out = timed(model)
+    clocks = sampler.stop()
+    ms_ref, out_ref = timed(ref)
+    finite = bool(torch.isfinite(out).all().item())
+    rel = float(((out.float() - out_ref.float()).norm() / out_ref.float().norm()).item())
+    # End to end: pinned host latent and conditioning in, predicted noise out.
+    hx, hctx = x.cpu().pin_memory(), ctx.cpu().pin_memory()
+    hextra = {k: v.cpu().pin_memory() for k, v in extra.items()}
+    hy = torch.empty_like(out, device="cpu").pin_memory()
+    h2d = hx.numel() * hx.element_size() + hctx.numel() * hctx.element_size() + sum(
+        v.numel() * v.element_size() for v in hextra.values())
+
+    def e2e_step():
+        ex = {k: v.to(device, non_blocking=True) for k, v in hextra.items()}
+        hy.copy_(step(model, hx.to(device, non_blocking=True), hctx.to(device, non_blocking=True),
+                      ex), non_blocking=True)
+
+    with torch.no_grad():
+        for _ in range(max(1, args.warmup)):
+            e2e_step()
+        barrier(dist)
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        for _ in range(args.steps):
+            e2e_step()
+        e.record()
+        torch.cuda.synchronize()
+    e2e_ms = max_over_ranks(dist, s.elapsed_time(e))
+    if rank == 0:
+        emit({
+            "metric": f"{name} UNet FP16 denoising step, latents/s ({n_rep} 3x3 s1 convs on NOVA F(6,3))",
+            "value": world * args.batch * args.steps / (ms / 1e3), "unit": "latents/s",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f16",
+            "data": "synthetic (N(0,1) latent and context, random timesteps, random-init weights)",
+            "config": {"workload": f"{args.workload}_unet_step", "batch_per_gpu": args.batch,
+                       "latent": [spec.in_ch, latent, latent],
+                       "parallelism": f"dp{world} (batch-partitioned)", "replaced_convs": n_rep,
+                       "l2": "activations and weights far larger than L2"},
+            "e2e": {"value": world * args.batch * args.steps / (e2e_ms / 1e3), "unit": "latents/s",
+                    "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": hy.numel() * hy.element_size()},
+            "gpu_launches": 3 * n_rep * args.steps,
+            "cudnn_same_model_latents_s": world * args.batch * args.steps / (ms_ref / 1e3),
+            "cudnn_same_model_ms_per_step": ms_ref / args.steps,
+            "output_finite": finite, "output_rel_diff_vs_cudnn": rel,
+            "clocks": clocks,
+        })
+    if dist is not None:
+        dist.destroy_process_group()
+
+
 def profile_stages(args):
     """Launch order: input transform, GEMM, output transform, repeated --steps
     times, for one sweep layer at --batch (reference counterpart:
@@ -741,21 +837,27 @@ def main():
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
-    ap.add_argument("--batch", type=int, default=128)
+    ap.add_argument("--batch", type=int, default=None,
+                    help="per-GPU batch; default 128 for sweep and resnet50, 8 for the UNet "
+                         "workloads")
     ap.add_argument("--cpu-batch", type=int, default=1)
     ap.add_argument("--impl", choices=["nova", "reference"], default="nova")
     ap.add_argument("--no-cpu", action="store_true")
-    ap.add_argument("--workload", choices=["sweep", "resnet50", "unet", "sdxl"], default="sweep",
+    ap.add_argument("--workload",
+                    choices=["sweep", "resnet50", "sd15", "sdxl", "sd15_layers", "sdxl_layers"],
+                    default="sweep",
                     help="sweep: ResNet-50 3x3 layer sweep (BASELINE config 2, default); "
-                         "resnet50: whole model images/s (config 3); unet: SD 1.5 UNet 3x3 "
-                         "layer shapes (config 4, per layer); sdxl: SDXL UNet 3x3 layer "
-                         "shapes (config 5, per layer)")
+                         "resnet50: whole model images/s (config 3); sd15 / sdxl: one UNet "
+                         "denoising step (configs 4 and 5); sd15_layers / sdxl_layers: their "
+                         "3x3 conv shapes one layer at a time against cuDNN")
     ap.add_argument("--fused", action="store_true",
                     help="with --profile-stages: run the fused single kernel instead (C, K <= 64)")
     ap.add_argument("--profile-stages", metavar="LAYER", default=None,
                     help="only run the three stage entries of one sweep layer (--steps times "
                          "each, no timing output): the driver for ncu captures")
     args = ap.parse_args()
+    if args.batch is None:
+        args.batch = 128 if args.workload in ("sweep", "resnet50") else 8
     if args.profile_stages:
         profile_stages(args)
         return
@@ -764,9 +866,12 @@ def main():
     elif args.workload == "resnet50":
         args.warmup = max(3, args.warmup)
         run_resnet50(args)
-    elif args.workload in ("unet", "sdxl"):
+    elif args.workload in ("sd15_layers", "sdxl_layers"):
         args.warmup = max(3, args.warmup)
         run_unet_layers(args)
+    elif args.workload in ("sd15", "sdxl"):
+        args.warmup = max(3, args.warmup)
+        run_unet_model(args)
     else:
         args.warmup = max(3, args.warmup)
         run_nova(args)
