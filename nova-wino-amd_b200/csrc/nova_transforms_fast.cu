@@ -626,7 +626,8 @@ __device__ __forceinline__ void bulk_load(uint32_t dst, const void* src, uint32_
 
 // kLand = 0: each warp loads channels cell by cell with 2-byte loads, two
 // channels per round (one memory round trip per round).  kLand = 2 (W even):
-// 4-byte loads of cell pairs, four channels per round.  kLand = 32 or 64: the
+// 4-byte loads of cell pairs, NOVA_PLANE_PAIR_CH channels per round.
+// kLand = 32 or 64: the
 // block's channels of one image are one contiguous span of x ([c][h][w]); it
 // lands in shared memory by bulk copies of kLand channels (one round trip
 // each) while the zero border of the padded plane is written, and is then
@@ -703,8 +704,8 @@ __global__ void __launch_bounds__(32 * PlaneGeo<TR, TC, kW>::kWarps, PlaneGeo<TR
     }
   } else if constexpr (kLand == 2) {
     // W even: one 4-byte load brings cells (w, w + 1) of a row of one
-    // channel, so a channel takes H*W/64 loads per lane and four channels fit
-    // a round.  The zero border is written once, not loaded.
+    // channel, so a channel takes H*W/64 loads per lane and several channels
+    // fit a round.  The zero border is written once, not loaded.
     const int HW2 = (H * W) >> 1;
     constexpr int kPairPer = (Pg::kCells / 2 + 31) / 32;
     int pofs[kPairPer];  // padded cell of the pair's first element, -1 past the plane
