@@ -601,7 +601,7 @@ def run_unet_layers(args):
         "ms_per_step": total_ms / args.steps, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "f16",
         "data": "synthetic (seeded N(0,1) FP16 inputs, Kaiming-normal FP32 weights)",
-        "config": {"workload": f"{args.workload}_unet_3x3_shapes", "layers": [l[0] for l in shapes],
+        "config": {"workload": f"{args.workload.split('_')[0]}_unet_3x3_shapes", "layers": [l[0] for l in shapes],
                    "batch_per_gpu": args.batch,
                    "l2": "flushed between steps (write then read 2x L2)"},
         "per_layer_vs_cudnn": vendor_layer_times(layers, flush),
