@@ -54,6 +54,8 @@ SDXL_LAYERS = [
 METRIC = "F(6,3) conv eff. TFLOP/s (direct-conv FLOPs / time), ResNet-50 3x3 s1 layer sweep"
 UNIT = "TFLOP/s"
 L2_BYTES = 126 * 1024 * 1024
+PARITY_TOL = 1e-2      # rel L2 against the oracle (tests/test_gpu_parity.py)
+ACCURACY_FACTOR = 1.1  # error vs FP64 direct conv <= 1.1x the oracle's
 
 
 def direct_flops(B, C, K, H):
@@ -143,7 +145,11 @@ def run_reference(args):
         v, threads, sample, _ = cpu_nova_sample(cpu_batch, seconds_budget=4.0)
         vals.append(v)
     value = statistics.median(vals)
-    flops_step = sum(direct_flops(cpu_batch, C, C, H) for _, C, H in LAYERS)
+    # The GPU arm's workload: every sweep layer at --batch per GPU.  Each step
+    # times a per-image sample of it (cpu_batch images of each layer); the
+    # metric is a throughput, so ms_per_step is that of the whole batch.
+    flops_step = sum(direct_flops(args.batch, C, C, H) for _, C, H in LAYERS)
+    world = int(os.environ.get("WORLD_SIZE", "1"))
     line = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT,
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
@@ -151,9 +157,11 @@ def run_reference(args):
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
         "data": "synthetic (seeded N(0,1) FP16 inputs, Kaiming-normal FP32 weights)",
         "config": {"workload": "resnet50_3x3_sweep", "layers": [l[0] for l in LAYERS],
-                   "batch_per_step": cpu_batch, "l2": "n/a (host)"},
+                   "batch_per_gpu": args.batch, "parallelism": f"dp{world} (batch-partitioned)",
+                   "l2": "n/a (host)"},
         "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port",
-                         "sample": sample},
+                         "sample": f"{sample}, i.e. {cpu_batch} of the {args.batch} images of "
+                                   "each layer per step", "cpu_model": cpu_model()},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
         "note": "reference is HIP/rocBLAS for MI300X and cannot run here; its NOVA math is "
                 "timed as the numpy restatement (oracle/nova_oracle.py) on the host cores",
@@ -362,7 +370,7 @@ def vendor_layer_times(layers, flush, reps=10):
 
 
 # DRAM bytes (read, write) per launch at batch 128, from one ncu capture of the
-# stage entries (profiles/dram_traffic_resnet50_sweep_b128.md gives the command).
+# stage entries (bench.py --profile-stages, one launch per kernel and layer).
 # ncu flushes the caches before each kernel and counts no write-back of lines
 # still dirty in L2 when the kernel ends, so the writes of V and M that stay in
 # the 126 MB L2 are missing here; the totals therefore sit below the algorithmic
@@ -530,6 +538,121 @@ def e2e_pipelined(hx, dx, hy, forwards, steps, cu, before_timing=None):
     return start.elapsed_time(end)
 
 
+def choose_e2e(serial_ms, pipe_ms, pipe_ok, note=None):
+    """Which end-to-end figure the line reports: the faster of the serial run
+    and the overlapped run, the overlapped one only when its outputs were
+    verified.  Returns (ms, mode, note)."""
+    serial_mode = "serial (one stream)"
+    pipe_mode = "copies overlapped (H2D / compute / D2H streams)"
+    if not pipe_ok:
+        return serial_ms, serial_mode, note or "overlapped run not verified; serial figure reported"
+    if pipe_ms <= serial_ms:
+        return pipe_ms, pipe_mode, note
+    return serial_ms, serial_mode, note or "overlapped run was slower; serial figure reported"
+
+
+def cpu_model():
+    try:
+        with open("/proc/cpuinfo") as f:
+            for line in f:
+                if line.startswith("model name"):
+                    return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    import platform
+    return platform.processor() or "unknown"
+
+
+def sample_indices(batch):
+    """Images whose outputs the parity check compares: the first two and the
+    last two of the batch."""
+    return sorted({0, min(1, batch - 1), max(0, batch - 2), batch - 1})
+
+
+def sample_parity(name, x, w, y):
+    """rel L2 of sampled output images against the CPU oracle's reference
+    precision NOVA math, and both errors against an FP64 direct convolution.
+    Runs outside every timed region (the oracle is the checker only)."""
+    import numpy as np
+    import nova_oracle as o
+    idx = sample_indices(x.shape[0])
+    xs = x[idx].cpu().numpy()
+    ws = w.detach().float().cpu().numpy()
+    ys = y[idx].cpu().numpy()
+    y_o = o.nova_forward(xs, ws, 1, "ref")
+    d = o.direct_conv_fp64(xs, ws, 1)
+    par, err, err_o = o.rel_l2(ys, y_o), o.rel_l2(ys, d), o.rel_l2(y_o, d)
+    finite = bool(np.isfinite(ys.astype(np.float32)).all())
+    return {"images": idx, "rel_l2_vs_oracle": round(par, 6), "rel_err_vs_fp64": round(err, 6),
+            "oracle_rel_err_vs_fp64": round(err_o, 6),
+            "ok": bool(finite and par <= PARITY_TOL and err <= ACCURACY_FACTOR * err_o)}
+
+
+def config2_grid(device, flush, batches=(1, 8, 32), reps=10):
+    """BASELINE config 2's grid below the main batch: every sweep layer at each
+    batch, L2 flushed before each launch, with torch's FP16 conv2d (cuDNN) on
+    the same layer and the sampled-image parity of the timed outputs."""
+    import torch
+    import torch.nn.functional as F
+    torch.backends.cudnn.benchmark = True
+    grid = {}
+    for B in batches:
+        for name, C, H, conv, x in build_layers(B, device):
+            w16 = conv.weight.detach().half()
+            with torch.no_grad():
+                for _ in range(3):
+                    F.conv2d(x, w16, padding=1)
+                ours = time_kernel(lambda: conv(x), reps, flush)
+                cud = time_kernel(lambda: F.conv2d(x, w16, padding=1), reps, flush)
+                y = conv(x)
+            fl = direct_flops(B, C, C, H)
+            grid.setdefault(name, {})[str(B)] = {
+                "us": round(ours * 1e3, 2), "eff_tflops": round(fl / ours / 1e9, 1),
+                "cudnn_fp16_us": round(cud * 1e3, 2),
+                "parity": sample_parity(name, x, conv.weight, y)}
+            del x, y
+    return grid
+
+
+def gemm_stage_b256(device, flush, peaks, reps=10):
+    """The north star's batch-256 GEMM stage: the tcgen05 GEMM alone (stage
+    entry nova_batched_gemm_v2, L2 flushed) at batch 256 for conv2_x, conv4_x
+    and conv5_x, with its fraction of the measured dense peak (burst figure:
+    the kernel is timed alone).  The same layers' whole forward at batch 256
+    is parity-checked on sampled images."""
+    import torch
+    from nova_winograd import ops
+    lib = ops.get_lib()
+    shapes = [l for l in LAYERS if l[0] in ("conv2_x", "conv4_x", "conv5_x")]
+    out = {}
+    for name, C, H, conv, x in build_layers(256, device, shapes):
+        nt = live_tiles(H)
+        BP = 256 * nt * nt
+        with torch.no_grad():
+            y = conv(x)
+        V = torch.empty(64, BP, C, dtype=torch.float16, device=device)
+        M = torch.empty(64, BP, C, dtype=torch.float16, device=device)
+        s = ops.stream_ptr()
+        ops.check(lib.nova_input_transform_v2(ops.ptr(x), ops.ptr(V), 256, C, H, H, 1, nt, nt, BP,
+                                              s), "input_transform")
+        h = conv._handle
+
+        def gm():
+            ops.check(lib.nova_batched_gemm_v2(h, ops.ptr(V), ops.ptr(M), BP, s), "gemm")
+
+        ms = time_kernel(gm, reps, flush)
+        flops = 2.0 * 64 * C * C * BP
+        tf = flops / ms / 1e9
+        out[name] = {"gemm_us": round(ms * 1e3, 2), "tflops": round(tf, 1),
+                     "frac_of_peak": round(tf / peaks["bf16_tflops"], 4),
+                     "peak": peaks["bf16_tflops"], "peak_kind": "dense bf16 burst (" +
+                     peaks["source"] + ")",
+                     "gemm_bytes": 2 * 64 * BP * C * 2 + 64 * C * C * 2,
+                     "parity": sample_parity(name, x, conv.weight, y)}
+        del V, M, x, y
+    return out
+
+
 def run_nova(args):
     import torch
     world, rank, local, dist = setup_dist()
@@ -614,24 +737,41 @@ def run_nova(args):
         e2e_note = f"overlapped run failed: {ex!r}; serial figure reported"
     all_ok = max_over_ranks(dist, 0.0 if ok else 1.0) == 0.0
     pipe_ms = max_over_ranks(dist, pipe_ms)
-    if all_ok:
-        e2e_ms, e2e_mode = pipe_ms, "copies overlapped (H2D / compute / D2H streams)"
-    else:
-        e2e_ms = serial_ms
-        if e2e_note is None:
-            e2e_note = "another rank's overlapped run failed; serial figure reported"
+    if not all_ok and e2e_note is None:
+        e2e_note = "another rank's overlapped run failed; serial figure reported"
+    e2e_ms, e2e_mode, e2e_note = choose_e2e(serial_ms, pipe_ms, all_ok, e2e_note)
     e2e_value = world * flops_step * args.steps / (e2e_ms / 1e3) / 1e12
 
-    stages = roofline = lat = cpu = vendor = None
+    # Parity of what was timed: sampled images of every layer's output on the
+    # timed inputs, against the oracle (after the timed region).
+    parity = None
+    if rank == 0:
+        with torch.no_grad():
+            parity = {name: sample_parity(name, x, conv.weight, conv(x))
+                      for name, C, H, conv, x in layers}
+
+    stages = roofline = lat = cpu = vendor = grid = b256 = None
     if rank == 0:
         stages = stage_profile(layers, batch, flush)
         roofline = roofline_from_stages(stages, peaks, batch)
         lat = b1_latency(device)
         vendor = vendor_layer_times(layers, flush)
+        if not args.quick:
+            grid = config2_grid(device, flush)
+            b256 = gemm_stage_b256(device, flush, peaks)
         if world == 1 and not args.no_cpu:
             v, threads, sample, extra = cpu_nova_sample(args.cpu_batch)
-            cpu = {"value": v, "unit": UNIT, "cores": threads, "kind": "port", "sample": sample}
+            cpu = {"value": v, "unit": UNIT, "cores": threads, "kind": "port", "sample": sample,
+                   "cpu_model": cpu_model()}
             cpu.update(extra)
+    barrier(dist)
+    # BASELINE config 3 on every rank (batch 256 per GPU), so the 1..N GPU
+    # runs record model images/s too.
+    r50 = None
+    if not args.quick:
+        del layers
+        torch.cuda.empty_cache()
+        r50 = resnet50_measure(256, max(3, args.steps // 2), 3, device, dist, world, rank)
     barrier(dist)
     if rank == 0:
         line = {
@@ -645,6 +785,7 @@ def run_nova(args):
             "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms / args.steps,
                     "mode": e2e_mode, "serial_ms_per_step": serial_ms / args.steps,
+                    "overlapped_ms_per_step": (pipe_ms / args.steps) if all_ok else None,
                     **({"note": e2e_note} if e2e_note else {})},
             "gpu_launches": launches,
             "roofline": roofline,
@@ -652,8 +793,12 @@ def run_nova(args):
             "cpu_baseline": cpu,
             "stages": [{k: (round(v, 5) if isinstance(v, float) else v) for k, v in st.items()}
                        for st in stages],
+            "parity": parity,
             "b1_latency_us": lat,
             "per_layer_vs_cudnn": vendor,
+            "config2_grid": grid,
+            "stages_b256": b256,
+            "resnet50": r50,
             "step_ms": [round(t, 4) for t in step_ms],
             "library": ops.get_lib().nova_version().decode(),
         }
@@ -708,25 +853,26 @@ def run_unet_layers(args):
     })
 
 
-def run_resnet50(args):
+def resnet50_measure(batch, steps, warmup, device, dist, world, rank):
     """torchvision ResNet-50 (random init, BN in eval mode
     with running mean 0 / var 1), FP16, 3x224x224 N(0,1) input; the 13 eligible
     3x3 stride-1 convs replaced by replace_conv2d_with_nova.  Data parallel by
-    batch: every rank runs --batch images per step (weak scaling).  The same
-    model without replacement (cuDNN) is timed alongside for context."""
+    batch: every rank runs `batch` images per step (weak scaling), timed with
+    CUDA events, max over ranks.  The same model without replacement (cuDNN) is
+    timed alongside; the replaced model's logits are compared with it, and one
+    image's output of every replaced conv with the CPU oracle.  All ranks call
+    this; returns the record (meaningful on rank 0)."""
     import torch
     import torchvision
-    from nova_winograd import replace_conv2d_with_nova
-    world, rank, local, dist = setup_dist()
-    device = torch.device("cuda", local)
+    from nova_winograd import NovaWinogradConv2d, replace_conv2d_with_nova
     torch.manual_seed(1234 + rank)
     ref = torchvision.models.resnet50().to(device).half().eval()
     model = torchvision.models.resnet50().to(device).half().eval()
     model.load_state_dict(ref.state_dict())
     n_rep = replace_conv2d_with_nova(model, verbose=False)
-    x = torch.randn(args.batch, 3, 224, 224, device=device, dtype=torch.float16)
+    x = torch.randn(batch, 3, 224, 224, device=device, dtype=torch.float16)
 
-    def timed(m, steps, warmup):
+    def timed(m):
         with torch.no_grad():
             for _ in range(warmup):
                 out = m(x)
@@ -739,44 +885,83 @@ def run_resnet50(args):
             torch.cuda.synchronize()
         return max_over_ranks(dist, s.elapsed_time(e)), out
 
-    uuid = str(torch.cuda.get_device_properties(device).uuid)
-    sampler = ClockSampler(uuid if uuid.startswith("GPU-") else f"GPU-{uuid}")
-    sampler.start()
-    ms, out = timed(model, args.steps, args.warmup)
-    clocks = sampler.stop()
-    ms_ref, out_ref = timed(ref, args.steps, args.warmup)
-    value = world * args.batch * args.steps / (ms / 1e3)
+    ms, out = timed(model)
+    ms_ref, out_ref = timed(ref)
     finite = bool(torch.isfinite(out).all().item())
     rel = float(((out.float() - out_ref.float()).norm() / out_ref.float().norm()).item())
     # End to end: pinned host images in, logits out, every step.
     hx = x.cpu().pin_memory()
-    hy = torch.empty(args.batch, 1000, dtype=torch.float16).pin_memory()
+    hy = torch.empty(batch, 1000, dtype=torch.float16).pin_memory()
     with torch.no_grad():
-        for _ in range(max(1, args.warmup)):
+        for _ in range(max(1, warmup)):
             hy.copy_(model(hx.to(device, non_blocking=True)), non_blocking=True)
         barrier(dist)
         s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         s.record()
-        for _ in range(args.steps):
+        for _ in range(steps):
             hy.copy_(model(hx.to(device, non_blocking=True)), non_blocking=True)
         e.record()
         torch.cuda.synchronize()
     e2e_ms = max_over_ranks(dist, s.elapsed_time(e))
+    rec = {
+        "img_s": world * batch * steps / (ms / 1e3), "ms_per_step": ms / steps,
+        "batch_per_gpu": batch, "n_gpus": world, "replaced_convs": n_rep,
+        "e2e": {"value": world * batch * steps / (e2e_ms / 1e3), "unit": "img/s",
+                "h2d_bytes_per_step": hx.numel() * 2, "d2h_bytes_per_step": hy.numel() * 2},
+        "cudnn_same_model_img_s": world * batch * steps / (ms_ref / 1e3),
+        "logits_finite": finite, "logits_rel_diff_vs_cudnn": rel,
+        "gpu_launches": 3 * n_rep * steps,
+    }
+    if rank == 0:
+        # Every replaced conv's output for image 0, from the activations the
+        # model feeds it, against the oracle (hooks outside the timed region).
+        seen = []
+        hooks = [mod.register_forward_hook(
+            lambda mod, inp, outp: seen.append((mod, inp[0][:1].clone(), outp[:1].clone())))
+            for mod in model.modules() if isinstance(mod, NovaWinogradConv2d)]
+        with torch.no_grad():
+            model(x[:1])
+        for hk in hooks:
+            hk.remove()
+        worst = None
+        for mod, xi, yi in seen:
+            r = sample_parity("resnet50", xi, mod.weight, yi)
+            if worst is None or r["rel_l2_vs_oracle"] > worst["rel_l2_vs_oracle"] or not r["ok"]:
+                worst = dict(r, ok=r["ok"] and (worst is None or worst["ok"]))
+        rec["conv_parity_image0"] = {"convs_checked": len(seen),
+                                     "worst_rel_l2_vs_oracle": worst["rel_l2_vs_oracle"],
+                                     "all_ok": worst["ok"]}
+    del model, ref, x
+    torch.cuda.empty_cache()
+    return rec
+
+
+def run_resnet50(args):
+    """--workload resnet50: the ResNet-50 record alone as the line."""
+    world, rank, local, dist = setup_dist()
+    import torch
+    device = torch.device("cuda", local)
+    uuid = str(torch.cuda.get_device_properties(device).uuid)
+    sampler = ClockSampler(uuid if uuid.startswith("GPU-") else f"GPU-{uuid}")
+    sampler.start()
+    rec = resnet50_measure(args.batch, args.steps, args.warmup, device, dist, world, rank)
+    clocks = sampler.stop()
     if rank == 0:
         emit({
             "metric": "ResNet-50 FP16 inference images/s (13 3x3 s1 convs on NOVA F(6,3))",
-            "value": value, "unit": "img/s", "n_gpus": world, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True,
+            "value": rec["img_s"], "unit": "img/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": rec["ms_per_step"], "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "f16",
             "data": "synthetic (N(0,1) images, random-init weights, BN eval mean 0 / var 1)",
             "config": {"workload": "resnet50", "batch_per_gpu": args.batch,
-                       "parallelism": f"dp{world} (batch-partitioned)", "replaced_convs": n_rep,
+                       "parallelism": f"dp{world} (batch-partitioned)",
+                       "replaced_convs": rec["replaced_convs"],
                        "l2": "activations far larger than L2"},
-            "e2e": {"value": world * args.batch * args.steps / (e2e_ms / 1e3), "unit": "img/s",
-                    "h2d_bytes_per_step": hx.numel() * 2, "d2h_bytes_per_step": hy.numel() * 2},
-            "gpu_launches": 3 * n_rep * args.steps,
-            "cudnn_same_model_img_s": world * args.batch * args.steps / (ms_ref / 1e3),
-            "logits_finite": finite, "logits_rel_diff_vs_cudnn": rel,
+            "e2e": rec["e2e"], "gpu_launches": rec["gpu_launches"],
+            "cudnn_same_model_img_s": rec["cudnn_same_model_img_s"],
+            "logits_finite": rec["logits_finite"],
+            "logits_rel_diff_vs_cudnn": rec["logits_rel_diff_vs_cudnn"],
+            "conv_parity_image0": rec.get("conv_parity_image0"),
             "clocks": clocks,
         })
     if dist is not None:
@@ -939,9 +1124,13 @@ def main():
     ap.add_argument("--batch", type=int, default=None,
                     help="per-GPU batch; default 128 for sweep and resnet50, 8 for the UNet "
                          "workloads")
-    ap.add_argument("--cpu-batch", type=int, default=1)
+    ap.add_argument("--cpu-batch", type=int, default=1,
+                    help="images of each layer the CPU legs time per pass (a sample of --batch)")
     ap.add_argument("--impl", choices=["nova", "reference"], default="nova")
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--quick", action="store_true",
+                    help="sweep only: skip the batch 1/8/32 grid, the batch-256 GEMM stage and "
+                         "the ResNet-50 record")
     ap.add_argument("--workload",
                     choices=["sweep", "resnet50", "sd15", "sdxl", "sd15_layers", "sdxl_layers"],
                     default="sweep",

@@ -88,7 +88,8 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
   uint64_t* empty = bars + kMaxStages;
   uint64_t* tfull = bars + 2 * kMaxStages;
   uint64_t* tempty = tfull + 2;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
+  uint64_t* drain = tempty + 2;  // MMA issuer: every MMA it issued has completed
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5;
@@ -103,6 +104,7 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
       mbar_init(smem_u32(&tfull[a]), 1);
       mbar_init(smem_u32(&tempty[a]), 128);
     }
+    mbar_init(smem_u32(drain), 1);
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
@@ -127,6 +129,7 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
       int s = 0;
       uint32_t ph = 0;
       bool ok = true;
+      long long issued = 0;
       for (long long t = blockIdx.x; t < p.total_tiles && ok; t += gridDim.x) {
         const int pos = (int)(t / tiles_per_pos);
         const long long rem = t % tiles_per_pos;
@@ -142,10 +145,24 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
           mbar_expect_tx(fb, stage_bytes);
           tma_load_3d(sa, &tmV, cb * kBK, bpt * kBM, pos, fb);
           tma_load_3d(sa + a_bytes, &tmU, cb * kBK, kt * p.BN, pos, fb);
+          ++issued;
           if (++s == S) {
             s = 0;
             ph ^= 1u;
           }
+        }
+      }
+      if (!ok) {
+        // Aborted: the last min(S, issued) stage loads may still be landing in
+        // shared memory.  Wait (bounded) for each one's completion before the
+        // CTA can exit and its shared memory be reused.
+        const long long n = issued < S ? issued : S;
+        for (long long i = 0; i < n; ++i) {
+          if (--s < 0) {
+            s = S - 1;
+            ph ^= 1u;
+          }
+          mbar_wait_drain(smem_u32(&full[s]), ph);
         }
       }
     }
@@ -188,6 +205,12 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
         }
         if (ok) umma_commit(smem_u32(&tfull[acc]));
       }
+      // Every MMA this thread issued completes before the commit below arrives.
+      // On the normal path the epilogue has already waited for all of them; on
+      // the abort path this keeps tcgen05.dealloc from freeing TMEM under MMAs
+      // still in flight.
+      umma_commit(smem_u32(drain));
+      mbar_wait_drain(smem_u32(drain), 0);
     }
   } else {
     // ---------------- Epilogue: warps 2..9 ----------------

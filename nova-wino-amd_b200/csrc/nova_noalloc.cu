@@ -17,6 +17,7 @@
 // stream capture).  Every call on a device shares the array: calls that overlap
 // on the GPU (different streams, no ordering) race on it.  Nothing in the array
 // needs clearing: each call writes every V and M element it later reads.
+#include <atomic>
 #include <string>
 
 #include "../../include/nova_winograd.h"
@@ -88,14 +89,17 @@ namespace {
 int noalloc_fail(int code, const std::string& msg) { return record_error(code, msg); }
 
 // Device address of the scratch array on the current device (looked up once).
+// Host threads may make their first calls concurrently: the slots are atomic,
+// and a racing lookup stores the same address.
 unsigned char* scratch_address(int* rc) {
-  static unsigned char* addr[64] = {};
+  static std::atomic<unsigned char*> addr[64] = {};
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) {
     *rc = noalloc_fail(NOVA_ERR_CUDA, "forward_noalloc: no usable current device");
     return nullptr;
   }
-  if (!addr[dev]) {
+  unsigned char* known = addr[dev].load(std::memory_order_relaxed);
+  if (!known) {
     void* p = nullptr;
     cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
     if (e != cudaSuccess) {
@@ -103,10 +107,11 @@ unsigned char* scratch_address(int* rc) {
                                             cudaGetErrorString(e));
       return nullptr;
     }
-    addr[dev] = static_cast<unsigned char*>(p);
+    known = static_cast<unsigned char*>(p);
+    addr[dev].store(known, std::memory_order_relaxed);
   }
   *rc = NOVA_OK;
-  return addr[dev];
+  return known;
 }
 }  // namespace
 

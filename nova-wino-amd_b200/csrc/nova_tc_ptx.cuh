@@ -67,6 +67,18 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatil
   }
 }
 
+// Bounded wait that ignores the abort flag: used after an abort, to let the
+// asynchronous copies and MMAs already issued finish before the CTA releases
+// its shared memory and TMEM.  Gives up silently after kDrainLimitNs.
+constexpr unsigned long long kDrainLimitNs = 500000000ull;  // 0.5 s
+__device__ __forceinline__ bool mbar_wait_drain(uint32_t bar, uint32_t parity) {
+  const uint64_t t0 = globaltimer();
+  for (uint32_t i = 0;; ++i) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if ((i & 255u) == 255u && globaltimer() - t0 > kDrainLimitNs) return false;
+  }
+}
+
 __device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap* map, int c0, int c1,
                                             int c2, uint32_t bar) {
   asm volatile(

@@ -232,6 +232,93 @@ def nova_forward(x: np.ndarray, w: np.ndarray, pad: int = 1, mode: str = "ref",
 
 
 # ---------------------------------------------------------------------------
+# The same three passes in the reference kernels' exact operation order.
+#
+# Each reference kernel accumulates its 8 (or 3x3) products one after another
+# in FP32, and the compiler contracts ``acc += a * b`` into a fused
+# multiply-add.  These restatements do the same, emulating each FMA in FP64
+# (the product of two FP32 numbers is exact there; the sum is then rounded to
+# FP32 -- a double rounding that differs from a true FMA with probability of
+# order 2^-29 per operation).  Their outputs match the reference kernels bit
+# for bit; the fast "ref" functions above differ from them only by FP32
+# summation order.
+# ---------------------------------------------------------------------------
+
+def _fma(acc, a, b):
+    """fl32(acc + a*b) with a single product rounding (FMA), elementwise."""
+    return (acc.astype(np.float64) + a.astype(np.float64) * b.astype(np.float64)).astype(np.float32)
+
+
+def filter_transform_seq(w: np.ndarray) -> np.ndarray:
+    """U[64][C][K] FP16 as filter_transform_kernel computes it
+    (csrc/nova_winograd.hip:243-254): for (p, q) in order,
+    result = fma(fl32(G[row][p] * w[p][q]), G^T[q][col], result)."""
+    _, _, G = matrices("ref")
+    K, C = w.shape[:2]
+    w = w.astype(np.float32)
+    acc = np.zeros((8, 8, K, C), dtype=np.float32)
+    for p in range(3):
+        for q in range(3):
+            t = (G[:, p][:, None, None] * w[None, :, :, p, q]).astype(np.float32)  # [row, K, C]
+            acc = _fma(acc, t[:, None], G[:, q][None, :, None, None])
+    return np.ascontiguousarray(acc.reshape(64, K, C).transpose(0, 2, 1)).astype(np.float16)
+
+
+def input_transform_seq(x: np.ndarray, nh: int, nw: int, pad: int) -> np.ndarray:
+    """V[64][B*P][C] FP16 as input_transform_kernel (csrc/nova_winograd.hip:181-199)
+    and input_transform_kernel_mt (:372-387) compute it:
+    temp[r][c] = sum_k fma(B^T[r][k], d[k][c]) in k order, then
+    V[r][c] = sum_k fma(temp[r][k], B[k][c]) in k order."""
+    _, Bm, _ = matrices("ref")
+    Bn, C = x.shape[:2]
+    d = input_tiles(x, nh, nw, pad)                       # [..., 8 (k), 8 (c)]
+    temp = np.zeros(d.shape, dtype=np.float32)
+    for k in range(8):
+        temp = _fma(temp, Bm[k, :][:, None], d[..., k:k + 1, :])      # B^T[r][k] = B[k][r]
+    v = np.zeros(d.shape, dtype=np.float32)
+    for k in range(8):
+        v = _fma(v, temp[..., :, k:k + 1], Bm[k, :][None, :])
+    v = v.transpose(4, 5, 0, 2, 3, 1).reshape(64, Bn * nh * nw, C)
+    return np.ascontiguousarray(v).astype(np.float16)
+
+
+def output_transform_seq(M: np.ndarray, Bn: int, nh: int, nw: int, H_out: int,
+                         W_out: int) -> np.ndarray:
+    """y FP16 NCHW as output_transform_kernel (csrc/nova_winograd.hip:305-327)
+    and output_transform_kernel_mt (:426-448) compute it:
+    temp[r][c] = sum_p fma(A[r][p], m[p][c]), y[r][c] = sum_p fma(temp[r][p], A^T[p][c])."""
+    A, _, _ = matrices("ref")
+    K = M.shape[2]
+    m = M.astype(np.float32).reshape(8, 8, Bn, nh, nw, K).transpose(2, 5, 3, 4, 0, 1)
+    temp = np.zeros(m.shape[:-2] + (6, 8), dtype=np.float32)
+    for p in range(8):
+        temp = _fma(temp, A[:, p][:, None], m[..., p:p + 1, :])
+    y = np.zeros(m.shape[:-2] + (6, 6), dtype=np.float32)
+    for p in range(8):
+        y = _fma(y, temp[..., :, p:p + 1], A[:, p][None, :])
+    y = y.astype(np.float16).transpose(0, 1, 2, 4, 3, 5).reshape(Bn, K, nh * 6, nw * 6)
+    return np.ascontiguousarray(y[:, :, :H_out, :W_out])
+
+
+def gemm_scale(U: np.ndarray, V: np.ndarray) -> np.ndarray:
+    """sum_c |V[pos][bp][c]| |U[pos][c][k]|: the magnitude that bounds the FP32
+    rounding of the GEMM's sums in any order."""
+    return np.matmul(np.abs(V.astype(np.float64)), np.abs(U.astype(np.float64)))
+
+
+def within_fp32_reordering(a: np.ndarray, b: np.ndarray, scale: np.ndarray,
+                           terms: int) -> np.ndarray:
+    """True where FP16 results a and b can both come from the same exact value
+    by FP32 sums of ``terms`` products taken in different orders and then
+    rounded to FP16: |a - b| <= one FP16 ulp at their magnitude plus
+    2 * terms * 2^-24 * scale (``scale`` = sum of the terms' magnitudes)."""
+    a64, b64 = a.astype(np.float64), b.astype(np.float64)
+    mag = np.maximum(np.abs(a64), np.abs(b64))
+    ulp16 = np.spacing(mag.astype(np.float16)).astype(np.float64)
+    return np.abs(a64 - b64) <= ulp16 + 2.0 * terms * 2.0 ** -24 * scale
+
+
+# ---------------------------------------------------------------------------
 # FP64 direct convolution (the accuracy yardstick) and the error metric.
 # ---------------------------------------------------------------------------
 

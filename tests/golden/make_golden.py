@@ -14,7 +14,8 @@ that runs here, and what this script turns into fixtures:
 * ``known_answers.json`` -- numbers the reference publishes for this path
   (FP16 relative error, test tolerances), with file:line.
 
-Usage:  python tests/golden/make_golden.py [/path/to/reference]
+Usage:  python tests/golden/make_golden.py <reference checkout>
+        (or set NOVA_REFERENCE_DIR)
 Nothing in the test suite runs this; the fixtures it wrote are committed.
 """
 
@@ -74,7 +75,9 @@ int main(void) {
 
 
 def main():
-    ref = sys.argv[1] if len(sys.argv) > 1 else "/root/reference"
+    ref = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("NOVA_REFERENCE_DIR")
+    if not ref:
+        sys.exit("usage: make_golden.py <reference checkout> (or set NOVA_REFERENCE_DIR)")
     path = os.path.join(ref, "csrc", "nova_winograd.hip")
     src = open(path).read()
 

@@ -111,3 +111,38 @@ def test_pipelined_e2e_outputs_and_ordering():
     assert len(waits_comp) == 3 * steps + 1
     assert waits_comp[-1].stream is s_out
     assert all(e.stream is s_in for e in waits_comp[:-1])
+
+
+def test_e2e_report_never_slower_than_serial():
+    """The reported end-to-end figure is the faster verified mode, and the mode
+    names the figure reported."""
+    cases = [(3.88, 6.92, True), (3.88, 2.10, True), (3.88, 2.10, False), (2.0, 2.0, True)]
+    for serial, pipe, ok in cases:
+        ms, mode, note = bench.choose_e2e(serial, pipe, ok)
+        assert ms <= serial
+        if ok and pipe <= serial:
+            assert ms == pipe and mode.startswith("copies overlapped") and note is None
+        else:
+            assert ms == serial and mode.startswith("serial") and note
+    # A failure note from the caller is kept.
+    assert bench.choose_e2e(1.0, 0.5, False, "boom")[2] == "boom"
+
+
+def test_parity_sample_indices():
+    assert bench.sample_indices(128) == [0, 1, 126, 127]
+    assert bench.sample_indices(1) == [0]
+    assert bench.sample_indices(2) == [0, 1]
+    assert bench.sample_indices(3) == [0, 1, 2]
+
+
+def test_sample_parity_flags_a_wrong_output():
+    import numpy as np
+    import nova_oracle as o
+    x, w = o.synthetic_case(4, 8, 8, 12, 12, seed=3)
+    y = o.nova_forward(x, w, 1, "ref")
+    xt, wt = torch.from_numpy(x), torch.from_numpy(w)
+    good = bench.sample_parity("t", xt, wt, torch.from_numpy(y))
+    assert good["ok"] and good["rel_l2_vs_oracle"] == 0.0 and good["images"] == [0, 1, 2, 3]
+    bad = y.copy()
+    bad[3, :, 5, 5] += np.float16(1.0)
+    assert not bench.sample_parity("t", xt, wt, torch.from_numpy(bad))["ok"]

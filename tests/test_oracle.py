@@ -187,3 +187,25 @@ def test_oracle_layouts_match_reference_kernel_loops():
     y_loop = _ref_output_transform_loops(M, 2, 2, Ho, Wo, nh, nw, BP)
     y_vec = o.output_transform(M, 2, nh, nw, Ho, Wo, "ref")
     assert _ulp_close(y_vec, y_loop)
+
+
+def test_exact_order_restatement_agrees_with_fast_oracle():
+    """The *_seq functions (the reference kernels' FMA chains in order) and the
+    vectorised "ref" functions differ only by FP32 summation order."""
+    x, w = o.synthetic_case(2, 8, 12, 11, 13, seed=9)
+    nh, nw, Ho, Wo = o.compute_tiling(11, 13, 1)
+    U, Us = o.filter_transform(w, "ref"), o.filter_transform_seq(w)
+    assert U.shape == Us.shape
+    _, _, G = o.matrices("ref")
+    sc = np.abs(G) @ np.abs(w).astype(np.float64) @ np.abs(G).T
+    sc = sc.transpose(2, 3, 1, 0).reshape(64, 8, 12)
+    assert o.within_fp32_reordering(Us, U, sc, 9).all()
+    V, Vs = o.input_transform(x, nh, nw, 1, "ref"), o.input_transform_seq(x, nh, nw, 1)
+    assert V.shape == Vs.shape and o.rel_l2(Vs, V) < 1e-3
+    M = o.gemm(U, V, "ref")
+    y, ys = o.output_transform(M, 2, nh, nw, Ho, Wo, "ref"), o.output_transform_seq(M, 2, nh, nw, Ho, Wo)
+    assert y.shape == ys.shape and o.rel_l2(ys, y) < 1e-3
+    # The reordering predicate rejects a real difference.
+    bad = ys.copy()
+    bad[0, 0, 0, 0] = np.float16(float(bad[0, 0, 0, 0]) + 0.5)
+    assert not o.within_fp32_reordering(bad, ys, np.zeros(ys.shape), 16).all()

@@ -54,6 +54,11 @@ def test_noalloc_matches_forward_twice_in_a_row():
         want = _reference_forward(lib, xd, wd, pad).cpu().numpy()
         assert np.isfinite(got.astype(np.float32)).all(), f"call {call}: NaN/Inf"
         assert o.rel_l2(got, want) <= PARITY_TOL, f"call {call}: rel L2 {o.rel_l2(got, want):.3e}"
+        # And against the CPU oracle, by the bars of the other parity tests.
+        y_o = o.nova_forward(x, w, pad, "ref")
+        d = o.direct_conv_fp64(x, w, pad)
+        assert o.rel_l2(got, y_o) <= PARITY_TOL, f"call {call}: vs oracle {o.rel_l2(got, y_o):.3e}"
+        assert o.rel_l2(got, d) <= 1.1 * o.rel_l2(y_o, d), f"call {call}: accuracy"
 
 
 def test_noalloc_refuses_shapes_beyond_its_scratch():
