@@ -386,8 +386,24 @@ cudaError_t tc_gemm_plan(TcGemmPlan* plan, const __half* U, int K, int C, const 
   // Narrower tiles for launches too small to fill the GPU with wide ones.
   plan->has_half = plan->BN > 128 && (plan->BN / 2) % 16 == 0 &&
                    tc::encode_operand_map(&plan->tmU_half, U, C, K, plan->BN / 2);
+  plan->has_pair = plan->BN % 64 == 0 &&
+                   tc::encode_operand_map(&plan->tmU_pair, U, C, K, plan->BN / 2);
   plan->valid = true;
   return cudaSuccess;
+}
+
+// SM-pair tiles pay off where the operands stream from L2 faster than one SM
+// can take them: wide channel counts, and enough pair tiles to fill the SMs.
+// NOVA_GEMM_PAIR=0 / 1 turns them off / on wherever eligible.
+static bool use_pair_gemm(const TcGemmPlan& plan, long long BP, int num_sms) {
+  static const int mode = [] {
+    const char* e = std::getenv("NOVA_GEMM_PAIR");
+    return e ? std::atoi(e) : -1;
+  }();
+  if (mode == 0 || !tc2_gemm_eligible(plan, BP)) return false;
+  if (mode == 1) return true;
+  const long long pair_tiles = 64ll * ((BP + 255) / 256) * (plan.K / plan.BN);
+  return plan.C >= 256 && plan.K >= 256 && pair_tiles >= num_sms / 2;
 }
 
 cudaError_t tc_gemm_run(const TcGemmPlan& plan, const __half* V, __half* M, long long BP,
@@ -401,6 +417,8 @@ cudaError_t tc_gemm_run(const TcGemmPlan& plan, const __half* V, __half* M, long
     *why = "V/M workspace not 16-byte aligned";
     return cudaErrorInvalidValue;
   }
+  if (use_pair_gemm(plan, BP, num_sms))
+    return tc2_gemm_run(plan, V, M, BP, dev_status, num_sms, s, why);
   CUtensorMap tmV;
   if (!tc::encode_operand_map(&tmV, V, plan.C, BP, tc::kBM)) {
     *why = "cuTensorMapEncodeTiled failed for V";

@@ -106,9 +106,12 @@ cudaError_t launch_gemm_simt(const __half* V, const __half* U, __half* M, long l
 struct TcGemmPlan {
   CUtensorMap tmU;       // U internal layout [64][K][C], box {64 c, BN k, 1}
   CUtensorMap tmU_half;  // the same with box {64 c, BN/2 k, 1} (BN > 128 only)
+  CUtensorMap tmU_pair;  // the same with box {64 c, BN/2 k, 1}: one CTA's half of
+                         // a pair tile (SM-pair GEMM, BN % 64 == 0 only)
   int BN = 0;            // output channels per tile (MMA N)
   int K = 0, C = 0;
   bool has_half = false;
+  bool has_pair = false;
   bool valid = false;
 };
 
@@ -119,6 +122,12 @@ cudaError_t tc_gemm_plan(TcGemmPlan* plan, const __half* U, int K, int C, const 
 // M[pos][bp][k] = sum_c V[pos][bp][c] U[pos][k][c] on the tensor cores.
 cudaError_t tc_gemm_run(const TcGemmPlan& plan, const __half* V, __half* M, long long BP,
                         int* dev_status, int num_sms, cudaStream_t s, const char** why);
+
+// The same GEMM on SM pairs (tcgen05 cta_group::2, 256 x BN pair tiles):
+// eligible launches and the launch itself (nova_gemm_tc2.cu).
+bool tc2_gemm_eligible(const TcGemmPlan& plan, long long BP);
+cudaError_t tc2_gemm_run(const TcGemmPlan& plan, const __half* V, __half* M, long long BP,
+                         int* dev_status, int num_sms, cudaStream_t s, const char** why);
 
 // 3-D FP16 tensor map over [64][rows][C] (C fastest), box {64, box_rows, 1},
 // SWIZZLE_128B: the layout of the UMMA K-major operands.
