@@ -392,18 +392,18 @@ cudaError_t tc_gemm_plan(TcGemmPlan* plan, const __half* U, int K, int C, const 
   return cudaSuccess;
 }
 
-// SM-pair tiles pay off where the operands stream from L2 faster than one SM
-// can take them: wide channel counts, and enough pair tiles to fill the SMs.
-// NOVA_GEMM_PAIR=0 / 1 turns them off / on wherever eligible.
+// SM-pair tiles (nova_gemm_tc2.cu) are opt-in: NOVA_GEMM_PAIR=1 uses them
+// wherever eligible.  Measured on the batch-256 and batch-128 conv4_x /
+// conv5_x GEMMs they are no faster than one SM per tile (conv5_x batch 256:
+// 38.9 us both ways; conv4_x batch 128: 24.6 against 20.5 us), so halving the
+// per-SM operand traffic does not relieve what bounds these launches.
 static bool use_pair_gemm(const TcGemmPlan& plan, long long BP, int num_sms) {
   static const int mode = [] {
     const char* e = std::getenv("NOVA_GEMM_PAIR");
-    return e ? std::atoi(e) : -1;
+    return e ? std::atoi(e) : 0;
   }();
-  if (mode == 0 || !tc2_gemm_eligible(plan, BP)) return false;
-  if (mode == 1) return true;
-  const long long pair_tiles = 64ll * ((BP + 255) / 256) * (plan.K / plan.BN);
-  return plan.C >= 256 && plan.K >= 256 && pair_tiles >= num_sms / 2;
+  (void)num_sms;
+  return mode == 1 && tc2_gemm_eligible(plan, BP);
 }
 
 cudaError_t tc_gemm_run(const TcGemmPlan& plan, const __half* V, __half* M, long long BP,

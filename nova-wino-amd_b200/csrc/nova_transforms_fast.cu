@@ -611,6 +611,17 @@ struct PlaneGeo {
   static constexpr size_t kOutSmem = (size_t)kOutCells * kPitch * 2;
 };
 
+// Zeroes a plane kernel's [kCells][kPitch] staging with 16-byte stores
+// (kCells = 4 (3TR + 1)(3TC + 1), so the plane is a whole number of 16-byte
+// words).  The caller orders it before other warps' writes with a barrier.
+template <class Pg>
+__device__ __forceinline__ void plane_zero_fill(__half* xs) {
+  constexpr int kWords = Pg::kCells * Pg::kPitch * 2 / 16;
+  static_assert(Pg::kCells * Pg::kPitch * 2 % 16 == 0, "plane not a multiple of 16 bytes");
+  uint4* z = reinterpret_cast<uint4*>(xs);
+  for (int i = threadIdx.x; i < kWords; i += 32 * Pg::kWarps) z[i] = make_uint4(0u, 0u, 0u, 0u);
+}
+
 // Plane args: BP/row window semantics as Args; row0 and lrow0 are tile rows and
 // are multiples of nh here (blocks own whole images).
 // Untiled bulk copy global -> shared, completing on an mbarrier (no multicast):
@@ -659,12 +670,18 @@ __global__ void __launch_bounds__(32 * PlaneGeo<TR, TC, kW>::kWarps, PlaneGeo<TR
       asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
     __syncthreads();
-    // Padded cell of each of the lane's image cells e = lane + 32 m.
+    // Padded cell of each of the lane's image cells e = lane + 32 m; only the
+    // first n_m rounds hold image cells.  Row h = floor(e / W) by one
+    // reciprocal: e < 2^10 and W <= 64, so (e + 1/2) / W sits at least 1/(2W)
+    // from an integer, far beyond the FP32 rounding of the product.
+    const int n_m = (HW + 31) >> 5;
+    const float rcp_w = 1.0f / (float)W;
     int cellofs[Pg::kInPerLane];
 #pragma unroll
     for (int m = 0; m < Pg::kInPerLane; ++m) {
       const int e = lane + 32 * m;
-      const int h = e / W, w = e - (e / W) * W;
+      const int h = __float2int_rz(((float)e + 0.5f) * rcp_w);
+      const int w = e - h * W;
       cellofs[m] = e < HW ? ((h + pad) * Pg::kCols + w + pad) * Pg::kPitch : -1;
     }
     uint32_t phase = 0;
@@ -678,13 +695,11 @@ __global__ void __launch_bounds__(32 * PlaneGeo<TR, TC, kW>::kWarps, PlaneGeo<TR
         bulk_load(land_s, xb + (long long)ch0 * HW, (uint32_t)(n * HW * 2), bar);
       }
       if (ch0 == 0) {
-        // Zero border cells (channel words 0..31) while the copy is in flight.
-        uint32_t* xw = reinterpret_cast<uint32_t*>(xs);
-        for (int cell = warp; cell < Pg::kCells; cell += Pg::kWarps) {
-          const int r = cell / Pg::kCols, col = cell - (cell / Pg::kCols) * Pg::kCols;
-          const int h = r - pad, w = col - pad;
-          if (h < 0 || h >= H || w < 0 || w >= W) xw[cell * (Pg::kPitch / 2) + lane] = 0u;
-        }
+        // Zero the whole staging plane with 16-byte stores while the copy is
+        // in flight (the border is most of it: 147 of 196 cells at 7 x 7); the
+        // barrier orders these stores before the interior writes below.
+        plane_zero_fill<Pg>(xs);
+        __syncthreads();
       }
       if (!mbar_wait_bounded(bar, phase)) return;
       phase ^= 1u;
@@ -694,6 +709,7 @@ __global__ void __launch_bounds__(32 * PlaneGeo<TR, TC, kW>::kWarps, PlaneGeo<TR
         const __half* s1 = s0 + HW;
 #pragma unroll
         for (int m = 0; m < Pg::kInPerLane; ++m) {
+          if (m >= n_m) break;
           const int e = lane + 32 * m;
           if (cellofs[m] >= 0)
             *reinterpret_cast<__half2*>(xs + cellofs[m] + ch0 + 2 * p2) =
@@ -708,19 +724,19 @@ __global__ void __launch_bounds__(32 * PlaneGeo<TR, TC, kW>::kWarps, PlaneGeo<TR
     // fit a round.  The zero border is written once, not loaded.
     const int HW2 = (H * W) >> 1;
     constexpr int kPairPer = (Pg::kCells / 2 + 31) / 32;
+    const int n_m = (HW2 + 31) >> 5;  // rounds that hold image cell pairs
+    const float rcp_w = 1.0f / (float)W;  // as in the bulk path: exact floor(e / W)
     int pofs[kPairPer];  // padded cell of the pair's first element, -1 past the plane
 #pragma unroll
     for (int m = 0; m < kPairPer; ++m) {
       const int e = 2 * (lane + 32 * m);
-      const int h = e / W, w = e - (e / W) * W;
+      const int h = __float2int_rz(((float)e + 0.5f) * rcp_w);
+      const int w = e - h * W;
       pofs[m] = e < 2 * HW2 ? ((h + pad) * Pg::kCols + w + pad) * Pg::kPitch : -1;
     }
-    uint32_t* xw = reinterpret_cast<uint32_t*>(xs);
-    for (int cell = warp; cell < Pg::kCells; cell += Pg::kWarps) {
-      const int r = cell / Pg::kCols, col = cell - (cell / Pg::kCols) * Pg::kCols;
-      const int h = r - pad, w = col - pad;
-      if (h < 0 || h >= H || w < 0 || w >= W) xw[cell * (Pg::kPitch / 2) + lane] = 0u;
-    }
+    // Zero the whole plane with 16-byte stores, then the interior is written.
+    plane_zero_fill<Pg>(xs);
+    __syncthreads();
     const uint32_t* xb2 = reinterpret_cast<const uint32_t*>(xb);
     constexpr int kCh = NOVA_PLANE_PAIR_CH;
     for (int cl0 = warp; cl0 < 64; cl0 += Pg::kWarps * kCh) {
@@ -731,8 +747,10 @@ __global__ void __launch_bounds__(32 * PlaneGeo<TR, TC, kW>::kWarps, PlaneGeo<TR
         const bool cok = cl < 64 && c0 + cl < C;
         const uint32_t* cp = xb2 + (cok ? cl : 0) * (long long)HW2;
 #pragma unroll
-        for (int m = 0; m < kPairPer; ++m)
+        for (int m = 0; m < kPairPer; ++m) {
+          if (m >= n_m) break;
           v[u][m] = (cok && pofs[m] >= 0) ? __ldg(cp + lane + 32 * m) : 0u;
+        }
       }
 #pragma unroll
       for (int u = 0; u < kCh; ++u) {
@@ -740,6 +758,7 @@ __global__ void __launch_bounds__(32 * PlaneGeo<TR, TC, kW>::kWarps, PlaneGeo<TR
         if (cl < 64) {
 #pragma unroll
           for (int m = 0; m < kPairPer; ++m) {
+            if (m >= n_m) break;
             if (pofs[m] >= 0) {
               xs[pofs[m] + cl] = __ushort_as_half((unsigned short)(v[u][m] & 0xffffu));
               xs[pofs[m] + Pg::kPitch + cl] = __ushort_as_half((unsigned short)(v[u][m] >> 16));
