@@ -588,10 +588,43 @@ def sample_parity(name, x, w, y):
             "ok": bool(finite and par <= PARITY_TOL and err <= ACCURACY_FACTOR * err_o)}
 
 
-def config2_grid(device, flush, batches=(1, 8, 32), reps=10):
-    """BASELINE config 2's grid below the main batch: every sweep layer at each
-    batch, L2 flushed before each launch, with torch's FP16 conv2d (cuDNN) on
-    the same layer and the sampled-image parity of the timed outputs."""
+def graph_of(fn):
+    """fn() captured once into a CUDA graph on a side stream."""
+    import torch
+    g = torch.cuda.CUDAGraph()
+    st = torch.cuda.Stream()
+    st.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(st):
+        fn()
+        st.synchronize()
+        with torch.cuda.graph(g, stream=st):
+            fn()
+    torch.cuda.current_stream().wait_stream(st)
+    torch.cuda.synchronize()
+    return g
+
+
+def back_to_back_us(fn, reps=100, warmup=20):
+    """Mean time of `reps` back-to-back calls between two events, L2 warm: the
+    reference's own per-layer method (benchmarks/bench_layers.py:18-30)."""
+    import torch
+    for _ in range(warmup):
+        fn()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    for _ in range(reps):
+        fn()
+    e.record()
+    torch.cuda.synchronize()
+    return s.elapsed_time(e) / reps * 1e3
+
+
+def config2_grid(device, flush, batches=(1, 8, 32, 128), reps=10):
+    """BASELINE config 2's grid: every sweep layer at each batch, with torch's FP16 conv2d (cuDNN) on the same layer and the
+    sampled-image parity of the timed outputs.  Per point: `us` = device time
+    of one forward replayed from a CUDA graph with L2 flushed before it (median);
+    `us_b2b` = the reference's method, back-to-back eager module calls with L2
+    warm (host submission included where it is the longer)."""
     import torch
     import torch.nn.functional as F
     torch.backends.cudnn.benchmark = True
@@ -602,15 +635,20 @@ def config2_grid(device, flush, batches=(1, 8, 32), reps=10):
             with torch.no_grad():
                 for _ in range(3):
                     F.conv2d(x, w16, padding=1)
-                ours = time_kernel(lambda: conv(x), reps, flush)
-                cud = time_kernel(lambda: F.conv2d(x, w16, padding=1), reps, flush)
+                g_ours = graph_of(lambda: conv(x))
+                g_cud = graph_of(lambda: F.conv2d(x, w16, padding=1))
+                ours = time_kernel(g_ours.replay, reps, flush)
+                cud = time_kernel(g_cud.replay, reps, flush)
+                ours_b2b = back_to_back_us(lambda: conv(x))
+                cud_b2b = back_to_back_us(lambda: F.conv2d(x, w16, padding=1))
                 y = conv(x)
             fl = direct_flops(B, C, C, H)
             grid.setdefault(name, {})[str(B)] = {
                 "us": round(ours * 1e3, 2), "eff_tflops": round(fl / ours / 1e9, 1),
                 "cudnn_fp16_us": round(cud * 1e3, 2),
+                "us_b2b": round(ours_b2b, 2), "cudnn_fp16_us_b2b": round(cud_b2b, 2),
                 "parity": sample_parity(name, x, conv.weight, y)}
-            del x, y
+            del x, y, g_ours, g_cud
     return grid
 
 
