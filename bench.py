@@ -287,8 +287,11 @@ def make_flush(device):
 
 
 def time_kernel(fn, reps, flush):
-    """Median device time (ms) of fn() with an L2 flush before each launch
-    (one untimed call first)."""
+    """Mean device time (ms) of fn() with an L2 flush before each launch (one
+    untimed call first).  CUDA event timestamps on this platform advance in
+    steps of about 2.05 us, so a median of single launches is quantised to that
+    step; the mean over launches whose start falls at random phases of the step
+    is not."""
     import torch
     fn()
     evs = []
@@ -300,10 +303,10 @@ def time_kernel(fn, reps, flush):
         e.record()
         evs.append((s, e))
     torch.cuda.synchronize()
-    return statistics.median(s.elapsed_time(e) for s, e in evs)
+    return statistics.mean(s.elapsed_time(e) for s, e in evs)
 
 
-def stage_profile(layers, batch, flush, reps=10):
+def stage_profile(layers, batch, flush, reps=20):
     """Per-stage device times through the stage C-ABI entries (one launch each,
     whole batch), with the algorithmic bytes / FLOPs of each launch."""
     import torch
@@ -346,7 +349,7 @@ def stage_profile(layers, batch, flush, reps=10):
     return out
 
 
-def vendor_layer_times(layers, flush, reps=10):
+def vendor_layer_times(layers, flush, reps=20):
     """Whole-layer device time of our forward and of torch's FP16 conv2d (cuDNN)
     on the same layer, L2 flushed before each launch (context, like the
     reference's MIOpen comparison in benchmarks/bench_layers.py)."""
@@ -619,10 +622,10 @@ def back_to_back_us(fn, reps=100, warmup=20):
     return s.elapsed_time(e) / reps * 1e3
 
 
-def config2_grid(device, flush, batches=(1, 8, 32, 128), reps=10):
+def config2_grid(device, flush, batches=(1, 8, 32, 128), reps=20):
     """BASELINE config 2's grid: every sweep layer at each batch, with torch's FP16 conv2d (cuDNN) on the same layer and the
     sampled-image parity of the timed outputs.  Per point: `us` = device time
-    of one forward replayed from a CUDA graph with L2 flushed before it (median);
+    of one forward replayed from a CUDA graph with L2 flushed before it (mean);
     `us_b2b` = the reference's method, back-to-back eager module calls with L2
     warm (host submission included where it is the longer)."""
     import torch
@@ -652,7 +655,7 @@ def config2_grid(device, flush, batches=(1, 8, 32, 128), reps=10):
     return grid
 
 
-def gemm_stage_b256(device, flush, peaks, reps=10):
+def gemm_stage_b256(device, flush, peaks, reps=20):
     """The north star's batch-256 GEMM stage: the tcgen05 GEMM alone (stage
     entry nova_batched_gemm_v2, L2 flushed) at batch 256 for conv2_x, conv4_x
     and conv5_x, with its fraction of the measured dense peak (burst figure:
