@@ -148,6 +148,28 @@ __device__ __forceinline__ void bt_1d2(const float2 v[8], float2 f[8]) {
   f[7] = fma2(-kB049, v[1], fma2(kB2211, v[3], fma2(-kB2721, v[5], v[7])));
 }
 
+// bt_1d2 split in two halves of its outputs, with exactly its operations:
+// rows {0, 1, 2, 7} and rows {3, 4, 5, 6}.  A 2-D transform that keeps only one
+// half of the column pass live at a time needs 64 registers instead of 128.
+__device__ __forceinline__ void bt_1d2_a(const float2 v[8], float2 f[4]) {
+  const float2 e1 = fma2(kB1361, v[2], fma2(-kB2361, v[4], v[6]));
+  const float2 o1 = fma2(kB0817, v[1], fma2(-kB1417, v[3], mul2(kB06, v[5])));
+  f[0] = fma2(-kB049, v[0], fma2(kB2211, v[2], fma2(-kB2721, v[4], v[6])));
+  f[1] = add2(e1, o1);
+  f[2] = sub2(e1, o1);
+  f[3] = fma2(-kB049, v[1], fma2(kB2211, v[3], fma2(-kB2721, v[5], v[7])));
+}
+__device__ __forceinline__ void bt_1d2_b(const float2 v[8], float2 f[4]) {
+  const float2 e2 = fma2(kB049, v[2], fma2(-kB1721, v[4], v[6]));
+  const float2 o2 = fma2(kB049, v[1], fma2(-kB1721, v[3], v[5]));
+  const float2 e3 = fma2(kB036, v[2], fma2(-kB1360, v[4], v[6]));
+  const float2 o3 = fma2(kB042, v[1], fma2(-kB1587, v[3], mul2(kB1167, v[5])));
+  f[0] = add2(e2, o2);
+  f[1] = sub2(e2, o2);
+  f[2] = add2(e3, o3);
+  f[3] = sub2(e3, o3);
+}
+
 __device__ __forceinline__ void a_1d2(const float2 m[8], float2 g[6]) {
   const float2 sa = add2(m[1], m[2]), da = sub2(m[1], m[2]);
   const float2 sb = add2(m[3], m[4]), db = sub2(m[3], m[4]);

@@ -435,6 +435,200 @@ __global__ void __launch_bounds__(32 * Geo<TPC, G>::kWarps, NOVA_IT_MIN_BLOCKS)
 #endif
 }
 
+// ---------------------------------------------------------------------------
+// Streaming input transform (W % 8 == 0, one 64-channel group per item).
+//
+// The block-per-item kernel above serialises, per block, TMA load -> transpose
+// -> transform -> store, and an SM holds three such blocks: its warps wait on
+// DRAM and on block barriers more than they compute.  This persistent kernel
+// (one CTA per SM) decouples the two.  Warp 0 streams the items' 8-row x
+// 64-channel landings by TMA into a ring of kSlots buffers; kGroups consumer
+// groups of TPC warps (one warp per tile) take items in turn: a group
+// transposes its landing into its own [col][channel slot][row] staging (the
+// landing slot is released right after, so the producer refills it while the
+// group computes), transforms one tile per warp and writes V with coalesced
+// 128-byte stores.  Items are (tile row, chunk of TPC tiles, 64 channels) in
+// the order of the block-per-item kernel's blocks.
+// ---------------------------------------------------------------------------
+// One 4-byte global store, kept in program order: as a plain C++ store the
+// compiler batches the 64 stores of a tile together with their 64-bit
+// addresses and spills at the 128-register cap.
+__device__ __forceinline__ void st_global_h2(__half2* p, __half2 v) {
+  asm volatile("st.global.b32 [%0], %1;" ::"l"(p), "r"(*reinterpret_cast<const uint32_t*>(&v))
+               : "memory");
+}
+
+template <int TPC>
+struct StreamGeo {
+  using Gm = Geo<TPC, 1>;
+  static constexpr int kGroups = 15 / TPC;       // 128 registers: 16 warps per SM
+  static constexpr int kWarps = 1 + kGroups * TPC;
+  static constexpr int kSlots = 3;
+  static constexpr size_t kLand = (Gm::kLandBytes + 127) / 128 * 128;
+  static constexpr size_t kXs = (Gm::kInSmemCol + 127) / 128 * 128;
+  static constexpr size_t kBars = 128;
+  static constexpr size_t kSmem = 128 + kSlots * kLand + kGroups * kXs + kBars;
+};
+
+template <int TPC>
+__global__ void __launch_bounds__(32 * StreamGeo<TPC>::kWarps, 1)
+    input_transform_stream(__half* __restrict__ V, const __grid_constant__ CUtensorMap map_x,
+                           const Args a, long long n_items) {
+  using Gm = Geo<TPC, 1>;
+  using Sg = StreamGeo<TPC>;
+  extern __shared__ uint8_t st_raw[];
+  uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(st_raw) + 127) &
+                                             ~uintptr_t(127));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(base + Sg::kSlots * Sg::kLand +
+                                               Sg::kGroups * Sg::kXs);
+  uint64_t* full = bars;
+  uint64_t* empty = bars + Sg::kSlots;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int C = a.C;
+  const int per_row = a.n_twc * ((C + Gm::kCGN - 1) / Gm::kCGN);
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < Sg::kSlots; ++i) {
+      tc::mbar_init(tc::smem_u32(&full[i]), 1);
+      tc::mbar_init(tc::smem_u32(&empty[i]), 1);
+    }
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+  }
+  __syncthreads();
+  pdl_wait();
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ---------------- TMA producer ----------------
+      long long j = 0;
+      for (long long item = blockIdx.x; item < n_items; item += gridDim.x, ++j) {
+        const int sl = (int)(j % Sg::kSlots);
+        const uint32_t ph = (uint32_t)((j / Sg::kSlots) & 1);
+        if (!mbar_wait_bounded(tc::smem_u32(&empty[sl]), ph ^ 1u)) break;
+        const long long lrow = item / per_row;
+        const int bx = (int)(item - lrow * per_row);
+        const int twc = bx % a.n_twc, cg = bx / a.n_twc;
+        const long long grow = a.row0 + lrow;
+        const int b = (int)(grow / a.nh), th = (int)(grow - (long long)b * a.nh);
+        const int w0 = twc * TPC * 6 - a.pad;
+        const int x0 = w0 >= 0 ? (w0 & ~7) : -((-w0 + 7) & ~7);
+        const uint32_t fb = tc::smem_u32(&full[sl]);
+        tc::mbar_expect_tx(fb, (uint32_t)Gm::kLandBytes);
+        tma_load_4d(tc::smem_u32(base + sl * Sg::kLand), &map_x, x0, th * 6 - a.pad,
+                    cg * Gm::kCGN, b, fb);
+      }
+    }
+  } else {
+    // ---------------- consumer groups ----------------
+    const int g = (warp - 1) / TPC, wg = (warp - 1) % TPC;
+    const uint32_t named = 1u + (uint32_t)g;  // barrier 0 is __syncthreads
+    __half* xs = reinterpret_cast<__half*>(base + Sg::kSlots * Sg::kLand + g * Sg::kXs);
+    const uint32_t xs_s = tc::smem_u32(xs);
+    const long long plane = a.BP * (long long)C;
+    long long j = 0;
+    for (long long item = blockIdx.x; item < n_items; item += gridDim.x, ++j) {
+      if ((int)(j % Sg::kGroups) != g) continue;
+      const int sl = (int)(j % Sg::kSlots);
+      const uint32_t ph = (uint32_t)((j / Sg::kSlots) & 1);
+      const long long lrow = item / per_row;
+      const int bx = (int)(item - lrow * per_row);
+      const int twc = bx % a.n_twc, cg = bx / a.n_twc;
+      const int c0 = cg * Gm::kCGN;
+      const int tw0 = twc * TPC;
+      const int ntw = min(TPC, a.nw - tw0);
+      const int w0 = tw0 * 6 - a.pad;
+      const int x0 = w0 >= 0 ? (w0 & ~7) : -((-w0 + 7) & ~7);
+      const int d = w0 - x0;
+      if (!mbar_wait_bounded(tc::smem_u32(&full[sl]), ph)) break;
+      // Transpose the landing [channel][row][col] into [col][channel slot][row]
+      // (as in input_transform_fast, mode 1), 8-column chunks over the group.
+      constexpr int kChunks = Gm::kBoxW / 8;
+      constexpr int kQuads = Gm::kCGN / 4;
+      const uint32_t land_s = tc::smem_u32(base + sl * Sg::kLand);
+      const uint32_t src_lane =
+          land_s + (uint32_t)((((lane >> 3) * 8 + (lane & 7)) * Gm::kBoxW) * 2);
+      for (int chunk = wg; chunk < kChunks; chunk += TPC) {
+        const int col = chunk * 8 + (lane >> 2) - d;
+        const bool in = col >= 0 && col < Gm::kInCols;
+        const uint32_t src = src_lane + (uint32_t)(chunk * 16);
+        const uint32_t dst =
+            xs_s + (uint32_t)(((in ? col : 0) * Gm::kColPitch + 2 * (lane & 3)) * 2);
+#pragma unroll
+        for (int cq = 0; cq < kQuads; ++cq) {
+          uint32_t rg[4];
+          asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0, %1, %2, %3}, [%4];"
+                       : "=r"(rg[0]), "=r"(rg[1]), "=r"(rg[2]), "=r"(rg[3])
+                       : "r"(src + (uint32_t)(cq * 4 * 8 * Gm::kBoxW * 2))
+                       : "memory");
+          if (in) {
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+              asm volatile("st.shared.b32 [%0], %1;" ::"r"(dst + (uint32_t)chan_slot(cq * 4 + i) * 16u),
+                           "r"(rg[i])
+                           : "memory");
+          }
+        }
+      }
+      asm volatile("bar.sync %0, %1;" ::"r"(named), "r"(32 * TPC) : "memory");
+      if (wg == 0 && lane == 0) tc::mbar_arrive(tc::smem_u32(&empty[sl]));  // landing read
+      const int t = wg;
+      if (t < ntw && c0 + 2 * lane < C) {  // C is even: a lane's pair is wholly in or out
+        const int cl = 2 * lane;
+        __half2* const vt = reinterpret_cast<__half2*>(V + (lrow * a.nw + tw0 + t) * C + c0 + cl);
+        const long long step = plane >> 1;  // one position plane of V, in half2
+        // The column pass in two halves of its output rows ({0,1,2,7} then
+        // {3,4,5,6}): 64 live registers for the intermediate instead of 128,
+        // at the cost of reading the staged columns twice.
+#pragma unroll 1
+        for (int half = 0; half < 2; ++half) {
+          float2 tt[4][8];
+#pragma unroll
+          for (int jc = 0; jc < 8; ++jc) {  // columns: tmp[.][jc] = B^T d[.][jc]
+            float2 v[8], f[4];
+            const __half* colp = xs + (t * 6 + jc) * Gm::kColPitch;
+            const uint4 wa = *reinterpret_cast<const uint4*>(colp + chan_slot(cl) * 8);
+            const uint4 wb = *reinterpret_cast<const uint4*>(colp + chan_slot(cl + 1) * 8);
+            const uint32_t ua[4] = {wa.x, wa.y, wa.z, wa.w}, ub[4] = {wb.x, wb.y, wb.z, wb.w};
+#pragma unroll
+            for (int i2 = 0; i2 < 4; ++i2) {
+              const float2 fa = __half22float2(*reinterpret_cast<const __half2*>(&ua[i2]));
+              const float2 fb = __half22float2(*reinterpret_cast<const __half2*>(&ub[i2]));
+              v[2 * i2] = make_float2(fa.x, fb.x);
+              v[2 * i2 + 1] = make_float2(fa.y, fb.y);
+            }
+            if (half == 0)
+              bt_1d2_a(v, f);
+            else
+              bt_1d2_b(v, f);
+#pragma unroll
+            for (int i = 0; i < 4; ++i) tt[i][jc] = f[i];
+          }
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {  // rows: V[r][.] = tmp[r][.] B
+            const int r = half == 0 ? (i < 3 ? i : 7) : 3 + i;
+            float2 f[8];
+            bt_1d2(tt[i], f);
+            __half2* out = vt + (long long)(r * 8) * step;
+#pragma unroll
+            for (int s2 = 0; s2 < 8; ++s2) {
+              st_global_h2(out, __float22half2_rn(f[s2]));
+              out += step;
+            }
+          }
+        }
+      }
+      // The staging is read by every warp of the group before the next item
+      // overwrites it.
+      asm volatile("bar.sync %0, %1;" ::"r"(named), "r"(32 * TPC) : "memory");
+    }
+  }
+  __syncthreads();
+  pdl_trigger();
+}
+
+template <int TPC>
+const void* it_stream_fn() { return (const void*)input_transform_stream<TPC>; }
+
 // kTmaIn: the block's M tiles ([pos][channels] each) arrive by TMA tile loads
 // into shared memory instead of 64 scattered 4-byte loads per lane.
 // kYTma (needs kTmaIn; W_out % 8 == 0 and TPC = 4, so every chunk starts on a
@@ -1183,6 +1377,29 @@ static bool encode_v_map(CUtensorMap* map, const __half* V, int C, long long BP,
   });
 }
 
+// The streaming input transform for TMA-staged rows, on unless NOVA_IT_STREAM=0.
+static bool it_stream_enabled() {
+  static const bool on = [] {
+    const char* e = std::getenv("NOVA_IT_STREAM");
+    return !(e && e[0] == '0');
+  }();
+  return on;
+}
+
+// SMs of the current device (persistent grids), looked up once per device.
+static int num_sms_cached() {
+  static int sms[64] = {};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
+  if (sms[dev] == 0) {
+    int n = 0;
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0)
+      n = 148;
+    sms[dev] = n;
+  }
+  return sms[dev];
+}
+
 template <int TPC, int G>
 static void launch_it(const __half* x, __half* V, Args a, long long nrows, unsigned gx,
                       cudaStream_t s) {
@@ -1203,6 +1420,18 @@ static void launch_it(const __half* x, __half* V, Args a, long long nrows, unsig
         smem_optin_once<it_pair_fn<TPC, G>>(kPairSmemMax)) {
       mode = 2;
       smem = pair_smem;
+    }
+  }
+  if constexpr (G == 1 && TPC >= 4 && TPC <= 6) {
+    if (mode == 1 && it_stream_enabled() &&
+        smem_optin_once<it_stream_fn<TPC>>(StreamGeo<TPC>::kSmem)) {
+      a.lrow0 = 0;
+      const long long n_items = nrows * (long long)gx;
+      const long long grid = std::min<long long>(n_items, num_sms_cached());
+      launch_pdl(kPdlInput, input_transform_stream<TPC>, dim3((unsigned)grid),
+                 dim3(32 * StreamGeo<TPC>::kWarps), StreamGeo<TPC>::kSmem, s, V, map, a,
+                 n_items);
+      return;
     }
   }
   for (long long done = 0; done < nrows; done += kMaxGridY) {
