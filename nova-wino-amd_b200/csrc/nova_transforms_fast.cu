@@ -837,8 +837,25 @@ __device__ __forceinline__ void bulk_load(uint32_t dst, const void* src, uint32_
 // lands in shared memory by bulk copies of kLand channels (one round trip
 // each) while the zero border of the padded plane is written, and is then
 // transposed into [cell][channel].  Needs C % 8 == 0 and a 16-byte aligned x.
+// Blocks per SM the plane input transform's register budget is sized for: as
+// many as its shared memory admits, up to a budget of 96 registers per thread
+// for the bulk-landed throughput shapes of at most 2 x 2 tiles (their staging
+// needs no per-lane cell tables and the column pass runs in halves), 128
+// registers otherwise.
 template <int TR, int TC, int kW, int kLand>
-__global__ void __launch_bounds__(32 * PlaneGeo<TR, TC, kW>::kWarps, PlaneGeo<TR, TC, kW>::kMinBlocks)
+constexpr int plane_it_min_blocks() {
+  using Pg = PlaneGeo<TR, TC, kW>;
+  constexpr size_t land = kLand >= 32 ? (size_t)kLand * Pg::kCells * 2 : 0;
+  constexpr int by_smem = (int)((227 * 1024) / (Pg::kInSmem + land + 1024));
+  constexpr int regs = (kW == 0 && kLand >= 32 && TR <= 2 && TC <= 2) ? 96 : 128;
+  constexpr int by_regs = 65536 / (regs * 32 * Pg::kWarps);
+  constexpr int n = by_smem < by_regs ? by_smem : by_regs;
+  return n < 1 ? 1 : n;
+}
+
+template <int TR, int TC, int kW, int kLand>
+__global__ void __launch_bounds__(32 * PlaneGeo<TR, TC, kW>::kWarps,
+                                  (plane_it_min_blocks<TR, TC, kW, kLand>()))
     input_transform_plane(const __half* __restrict__ x, __half* __restrict__ V, const Args a) {
   using Pg = PlaneGeo<TR, TC, kW>;
   extern __shared__ __align__(16) __half xs[];  // [kCells][kPitch], then the landing
@@ -1004,27 +1021,41 @@ __global__ void __launch_bounds__(32 * PlaneGeo<TR, TC, kW>::kWarps, PlaneGeo<TR
     const int tr = t / TC, tc = t - (t / TC) * TC;
     const int cl = 2 * lane;
     const int c = c0 + cl;
-    float2 tt[8][8];
+    if (c >= C) continue;  // C is even: the lane's pair is wholly in or out
+    const long long bp = (limg * TR + tr) * TC + tc;
+    __half2* const vt = reinterpret_cast<__half2*>(V + bp * C + c);
+    const long long step = plane >> 1;  // one position plane of V, in half2
+    const __half* tile_s = xs + ((tr * 6) * Pg::kCols + tc * 6) * Pg::kPitch + cl;
+    // Column pass in two halves of its output rows ({0,1,2,7}, {3,4,5,6}):
+    // 64 live registers for the intermediate instead of 128 (no spills).
+#pragma unroll 1
+    for (int half = 0; half < 2; ++half) {
+      float2 tt[4][8];
 #pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      float2 v[8], f[8];
+      for (int j = 0; j < 8; ++j) {
+        float2 v[8], f[4];
 #pragma unroll
-      for (int i = 0; i < 8; ++i)
-        v[i] = __half22float2(*reinterpret_cast<const __half2*>(
-            xs + ((tr * 6 + i) * Pg::kCols + tc * 6 + j) * Pg::kPitch + cl));
-      bt_1d2(v, f);
+        for (int i = 0; i < 8; ++i)
+          v[i] = __half22float2(
+              *reinterpret_cast<const __half2*>(tile_s + (i * Pg::kCols + j) * Pg::kPitch));
+        if (half == 0)
+          bt_1d2_a(v, f);
+        else
+          bt_1d2_b(v, f);
 #pragma unroll
-      for (int i = 0; i < 8; ++i) tt[i][j] = f[i];
-    }
-    if (c < C) {
-      const long long bp = (limg * TR + tr) * TC + tc;
-      __half2* out = reinterpret_cast<__half2*>(V + bp * C + c);
+        for (int i = 0; i < 4; ++i) tt[i][j] = f[i];
+      }
 #pragma unroll
-      for (int r = 0; r < 8; ++r) {
+      for (int i = 0; i < 4; ++i) {
+        const int r = half == 0 ? (i < 3 ? i : 7) : 3 + i;
         float2 f[8];
-        bt_1d2(tt[r], f);
+        bt_1d2(tt[i], f);
+        __half2* out = vt + (long long)(r * 8) * step;
 #pragma unroll
-        for (int s = 0; s < 8; ++s) out[(long long)(r * 8 + s) * (plane >> 1)] = __float22half2_rn(f[s]);
+        for (int s = 0; s < 8; ++s) {
+          st_global_h2(out, __float22half2_rn(f[s]));
+          out += step;
+        }
       }
     }
   }
