@@ -413,3 +413,16 @@ def _wrap_device_ptr(p, n):
         __cuda_array_interface__ = {"shape": (n,), "typestr": "<f2", "data": (p, False),
                                     "version": 3, "strides": None}
     return torch.as_tensor(_Holder(), device="cuda")
+
+
+@pytest.mark.parametrize("B,C,K,H", [(16, 64, 64, 56), (40, 256, 256, 14), (6, 128, 96, 28)])
+def test_l2_windowed_three_pass_matches_single_window(B, C, K, H):
+    # The batch cut into windows of whole tile rows whose V + M fit an 8 MB
+    # budget (NOVA_L2_WINDOW_MB, reference tests/test_bp_tiled.hip:482-571):
+    # every tile is computed by the same kernels, so the bytes are the same.
+    x, w = o.synthetic_case(B, C, K, H, H, seed=808 + C + H)
+    y, _ = run_forward(x, w, 1)
+    yw = forward_in_child(x, w, 1, {"NOVA_L2_WINDOW_MB": "8"})
+    np.testing.assert_array_equal(y, yw)
+    check_parity(x[:2], w, 1, yw[:2])
+    check_parity(x[-2:], w, 1, yw[-2:])
