@@ -154,6 +154,20 @@ int nova_device_status(nova_handle_t h);
 int nova_forward_noalloc(const void* d_input, const void* d_U_gemm, void* d_output, int batch,
                          int C, int K, int H, int W, int pad, void* stream);
 
+/* Weight gradient of the 3x3 stride-1 convolution by the NOVA F(6,3) Winograd
+ * algorithm, replacing the reference's FP32 per-sample unfold loop
+ * (nova_winograd/conv2d.py:131-141 and the custom-op backward :66-80):
+ * dW[K][C][3][3] (FP32) from the FP16 input x [B][C][H][W] and output gradient
+ * dy [B][K][H_out][W_out].  dW = G^T [sum over tiles (A^T dY A) . (B^T d B)] G:
+ * both transforms stored FP16, the per-position sums over tiles on the tensor
+ * cores with FP32 accumulation.  C must be a multiple of 16.  The caller passes
+ * a 256-byte aligned device workspace of nova_weight_grad_workspace_bytes()
+ * bytes; nothing is allocated.  Runs on `stream`; returns a NOVA_* status. */
+long long nova_weight_grad_workspace_bytes(int batch, int C, int K, int H, int W, int pad);
+int nova_weight_grad_v2(const void* d_input, const void* d_grad_output, void* d_grad_weight,
+                        void* d_workspace, long long workspace_bytes, int batch, int C, int K,
+                        int H, int W, int pad, void* stream);
+
 /* Library version string. */
 const char* nova_version(void);
 

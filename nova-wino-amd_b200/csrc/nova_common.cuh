@@ -77,6 +77,27 @@ __device__ __forceinline__ void bt_1d(const float v[8], float f[8]) {
   f[7] = fmaf(-kB049, v[1], fmaf(kB2211, v[3], fmaf(-kB2721, v[5], v[7])));
 }
 
+// bt_1d split in two halves of its outputs with exactly its operations: rows
+// {0, 1, 2, 7} and rows {3, 4, 5, 6}.
+__device__ __forceinline__ void bt_1d_a(const float v[8], float f[4]) {
+  const float e1 = fmaf(kB1361, v[2], fmaf(-kB2361, v[4], v[6]));
+  const float o1 = fmaf(kB0817, v[1], fmaf(-kB1417, v[3], kB06 * v[5]));
+  f[0] = fmaf(-kB049, v[0], fmaf(kB2211, v[2], fmaf(-kB2721, v[4], v[6])));
+  f[1] = e1 + o1;
+  f[2] = e1 - o1;
+  f[3] = fmaf(-kB049, v[1], fmaf(kB2211, v[3], fmaf(-kB2721, v[5], v[7])));
+}
+__device__ __forceinline__ void bt_1d_b(const float v[8], float f[4]) {
+  const float e2 = fmaf(kB049, v[2], fmaf(-kB1721, v[4], v[6]));
+  const float o2 = fmaf(kB049, v[1], fmaf(-kB1721, v[3], v[5]));
+  const float e3 = fmaf(kB036, v[2], fmaf(-kB1360, v[4], v[6]));
+  const float o3 = fmaf(kB042, v[1], fmaf(-kB1587, v[3], kB1167 * v[5]));
+  f[0] = e2 + o2;
+  f[1] = e2 - o2;
+  f[2] = e3 + o3;
+  f[3] = e3 - o3;
+}
+
 // A[i][p] (6 x 8, FP16-rounded entries) as a table, for code that indexes A
 // rather than running the butterfly.
 __host__ __device__ constexpr float kA(int i, int p) {

@@ -45,14 +45,32 @@ constexpr int kSmemLimit = (227 * 1024) / kCtasPerSm - (kCtasPerSm > 1 ? 1024 : 
 
 struct Params {
   __half* M;
+  float* Mf;       // non-null: FP32 output, accumulated with atomic adds (split reduction)
   long long BP;
   int C, K, BN;
   int n_bp_tiles, n_k_tiles, n_cblk;
+  int n_split;     // the reduction's 64-channel blocks split into n_split ranges
+  int kb_per_split;
   long long total_tiles;
   int stages;
   int tma_store;  // 1: epilogue stages 32-row slabs in smem and TMA-stores them
   int* status;
 };
+
+// Tile t -> (pos, bp tile, k tile) and its range of reduction blocks.  The
+// split index runs fastest, so with one split the order is (pos, bp, k).
+__device__ __forceinline__ void tile_of(const Params& p, long long t, int& pos, int& bpt, int& kt,
+                                        int& cb0, int& cb1) {
+  const int split = (int)(t % p.n_split);
+  t /= p.n_split;
+  const long long per_pos = (long long)p.n_bp_tiles * p.n_k_tiles;
+  pos = (int)(t / per_pos);
+  const long long rem = t % per_pos;
+  bpt = (int)(rem / p.n_k_tiles);
+  kt = (int)(rem % p.n_k_tiles);
+  cb0 = split * p.kb_per_split;
+  cb1 = min(p.n_cblk, cb0 + p.kb_per_split);
+}
 
 // FP32 accumulator bits -> FP16, written as kVec 16-byte stores (8 columns each).
 template <int kVec>
@@ -120,7 +138,6 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
-  const long long tiles_per_pos = (long long)p.n_bp_tiles * p.n_k_tiles;
   pdl_wait();  // V (and U) come from earlier kernels in the stream
 
   if (warp == 0) {
@@ -131,11 +148,9 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
       bool ok = true;
       long long issued = 0;
       for (long long t = blockIdx.x; t < p.total_tiles && ok; t += gridDim.x) {
-        const int pos = (int)(t / tiles_per_pos);
-        const long long rem = t % tiles_per_pos;
-        const int bpt = (int)(rem / p.n_k_tiles);
-        const int kt = (int)(rem % p.n_k_tiles);
-        for (int cb = 0; cb < p.n_cblk; ++cb) {
+        int pos, bpt, kt, cb0, cb1;
+        tile_of(p, t, pos, bpt, kt, cb0, cb1);
+        for (int cb = cb0; cb < cb1; ++cb) {
           if (!mbar_wait(smem_u32(&empty[s]), ph ^ 1u, abort_flag, p.status, kDevTimeoutProducer)) {
             ok = false;
             break;
@@ -182,7 +197,9 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
           break;
         tc_fence_after();
         const uint32_t dcol = tmem_base + acc * (uint32_t)p.BN;
-        for (int cb = 0; cb < p.n_cblk; ++cb) {
+        int pos_, bpt_, kt_, cb0, cb1;
+        tile_of(p, t, pos_, bpt_, kt_, cb0, cb1);
+        for (int cb = cb0; cb < cb1; ++cb) {
           if (!mbar_wait(smem_u32(&full[s]), ph, abort_flag, p.status, kDevTimeoutMma)) {
             ok = false;
             break;
@@ -195,7 +212,7 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
           for (int k = 0; k < kBK / kUmmaK; ++k) {
             // +32 bytes along K inside the swizzled 128-byte row = +2 in the
             // descriptor's 16-byte address units.
-            umma_f16(dcol, ad + 2ull * k, bd + 2ull * k, idesc, (cb | k) != 0);
+            umma_f16(dcol, ad + 2ull * k, bd + 2ull * k, idesc, (cb != cb0) || (k != 0));
           }
           umma_commit(smem_u32(&empty[s]));
           if (++s == S) {
@@ -222,10 +239,8 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
     uint32_t it = eg;
     for (long long t = blockIdx.x + (long long)eg * gridDim.x; t < p.total_tiles;
          t += 2ll * gridDim.x, it += 2) {
-      const int pos = (int)(t / tiles_per_pos);
-      const long long rem = t % tiles_per_pos;
-      const int bpt = (int)(rem / p.n_k_tiles);
-      const int kt = (int)(rem % p.n_k_tiles);
+      int pos, bpt, kt, cb0_, cb1_;
+      tile_of(p, t, pos, bpt, kt, cb0_, cb1_);
       const uint32_t acc = it & 1u;
       const uint32_t aph = (it >> 1) & 1u;
       if (!mbar_wait(smem_u32(&tfull[acc]), aph, abort_flag, p.status, kDevTimeoutEpilogue)) break;
@@ -271,6 +286,22 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
         continue;
       }
       const long long bp = (long long)bpt * kBM + row;
+      if (p.Mf) {
+        // FP32 partial sums of this tile's reduction range, added into the
+        // output (other splits of the same tile add theirs).
+        float* outf = p.Mf + ((long long)pos * p.BP + bp) * p.K + (long long)kt * p.BN;
+        for (int j = 0; j < p.BN; j += 16) {
+          uint32_t r[16];
+          tmem_ld16(taddr + j, r);
+          if (bp < p.BP) {
+#pragma unroll
+            for (int q = 0; q < 16; ++q) atomicAdd(outf + j + q, __uint_as_float(r[q]));
+          }
+        }
+        tc_fence_before();
+        mbar_arrive(smem_u32(&tempty[acc]));
+        continue;
+      }
       __half* out = p.M + ((long long)pos * p.BP + bp) * p.K + (long long)kt * p.BN;
       int j = 0;
       for (; j + 32 <= p.BN; j += 32) {
@@ -440,6 +471,7 @@ cudaError_t tc_gemm_run(const TcGemmPlan& plan, const __half* V, __half* M, long
   p.tma_store = (BN % 64) == 0 &&
                 tc::encode_operand_map(&tmM, M, plan.K, BP, 32);
   p.M = M;
+  p.Mf = nullptr;
   p.BP = BP;
   p.C = plan.C;
   p.K = plan.K;
@@ -447,6 +479,8 @@ cudaError_t tc_gemm_run(const TcGemmPlan& plan, const __half* V, __half* M, long
   p.n_bp_tiles = (int)((BP + tc::kBM - 1) / tc::kBM);
   p.n_k_tiles = plan.K / BN;
   p.n_cblk = (plan.C + tc::kBK - 1) / tc::kBK;
+  p.n_split = 1;
+  p.kb_per_split = p.n_cblk;
   p.total_tiles = 64ll * p.n_bp_tiles * p.n_k_tiles;
   p.status = dev_status;
   const int stage_bytes = tc::kBM * tc::kBK * 2 + BN * tc::kBK * 2;
@@ -477,6 +511,84 @@ cudaError_t tc_gemm_run(const TcGemmPlan& plan, const __half* V, __half* M, long
   cudaError_t e = launch_pdl(kPdlGemm, tc::gemm_tc_kernel, dim3((unsigned)grid), dim3(tc::kThreads), smem, s,
                              tmV, *tmU, tmM, p);
   if (e != cudaSuccess) *why = "tensor-core GEMM launch failed";
+  return e;
+}
+
+// Weight-gradient GEMM (nova_wgrad.cu): Ug[pos][K][C] += sum over bp of
+// A[pos][K][bp] * Bop[pos][C][bp], both operands with the reduction (bp)
+// contiguous at a row pitch of `pitch` halves, FP32 output by atomic adds.
+// The reduction is split over enough CTAs to fill the GPU; Ug must be zeroed.
+static bool encode_pitched_map(CUtensorMap* map, const void* ptr, long long inner,
+                               long long pitch, long long rows, int box_rows) {
+  tc::EncodeTiledFn fn = tc::get_encode_fn();
+  if (!fn) return false;
+  cuuint64_t dims[3] = {(cuuint64_t)inner, (cuuint64_t)rows, 64};
+  cuuint64_t strides[2] = {(cuuint64_t)pitch * 2, (cuuint64_t)pitch * 2 * (cuuint64_t)rows};
+  cuuint32_t box[3] = {(cuuint32_t)tc::kBK, (cuuint32_t)box_rows, 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  return fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, const_cast<void*>(ptr), dims, strides, box,
+            estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+cudaError_t tc_gemm_wgrad_run(const __half* A, const __half* Bop, float* Ug, int K, int C,
+                              long long BP, long long pitch, int* dev_status, int num_sms,
+                              cudaStream_t s, const char** why) {
+  const int BN = tc::pick_bn(C);
+  if (BN == 0 || K <= 0 || BP <= 0 || pitch % 8 || pitch < BP) {
+    *why = "weight-gradient GEMM: unsupported shape";
+    return cudaErrorInvalidValue;
+  }
+  if (reinterpret_cast<uintptr_t>(A) % 16 || reinterpret_cast<uintptr_t>(Bop) % 16) {
+    *why = "weight-gradient GEMM: operands not 16-byte aligned";
+    return cudaErrorInvalidValue;
+  }
+  CUtensorMap tmA, tmB, tmNone;
+  std::memset(&tmNone, 0, sizeof(tmNone));
+  if (!encode_pitched_map(&tmA, A, BP, pitch, K, tc::kBM) ||
+      !encode_pitched_map(&tmB, Bop, BP, pitch, C, BN)) {
+    *why = "cuTensorMapEncodeTiled failed for the weight-gradient operands";
+    return cudaErrorInvalidValue;
+  }
+  tc::Params p;
+  p.M = nullptr;
+  p.Mf = Ug;
+  p.BP = K;  // rows of the output
+  p.C = (int)std::min<long long>(BP, 1ll << 30);
+  p.K = C;   // columns of the output
+  p.BN = BN;
+  p.n_bp_tiles = (K + tc::kBM - 1) / tc::kBM;
+  p.n_k_tiles = C / BN;
+  p.n_cblk = (int)((BP + tc::kBK - 1) / tc::kBK);
+  const long long base = 64ll * p.n_bp_tiles * p.n_k_tiles;
+  int n_split = (int)std::min<long long>(p.n_cblk, (2ll * num_sms + base - 1) / base);
+  if (n_split < 1) n_split = 1;
+  p.kb_per_split = (p.n_cblk + n_split - 1) / n_split;
+  p.n_split = (p.n_cblk + p.kb_per_split - 1) / p.kb_per_split;
+  p.total_tiles = base * p.n_split;
+  p.tma_store = 0;
+  p.status = dev_status;
+  const int stage_bytes = tc::kBM * tc::kBK * 2 + BN * tc::kBK * 2;
+  const int overhead = 1024 + 256;
+  p.stages = std::min(tc::kMaxStages, (tc::kSmemLimit - overhead) / stage_bytes);
+  const int smem = overhead + p.stages * stage_bytes;
+  static bool configured[64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64 || !configured[dev]) {
+    cudaError_t e = cudaFuncSetAttribute(tc::gemm_tc_kernel,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         tc::kSmemLimit);
+    if (e != cudaSuccess) {
+      *why = "cudaFuncSetAttribute(MaxDynamicSharedMemorySize) failed";
+      return e;
+    }
+    if (dev >= 0 && dev < 64) configured[dev] = true;
+  }
+  const long long grid = std::min<long long>(p.total_tiles, (long long)num_sms * tc::kCtasPerSm);
+  cudaError_t e = launch_pdl(kPdlGemm, tc::gemm_tc_kernel, dim3((unsigned)grid),
+                             dim3(tc::kThreads), smem, s, tmA, tmB, tmNone, p);
+  if (e != cudaSuccess) *why = "weight-gradient GEMM launch failed";
   return e;
 }
 

@@ -129,6 +129,13 @@ bool tc2_gemm_eligible(const TcGemmPlan& plan, long long BP);
 cudaError_t tc2_gemm_run(const TcGemmPlan& plan, const __half* V, __half* M, long long BP,
                          int* dev_status, int num_sms, cudaStream_t s, const char** why);
 
+// Weight-gradient GEMM: Ug[pos][K][C] += sum_bp A[pos][K][bp] * Bop[pos][C][bp]
+// (rows `pitch` halves apart, bp < BP valid), FP32 atomic adds, reduction split
+// over CTAs.  Ug must be zeroed first.
+cudaError_t tc_gemm_wgrad_run(const __half* A, const __half* Bop, float* Ug, int K, int C,
+                              long long BP, long long pitch, int* dev_status, int num_sms,
+                              cudaStream_t s, const char** why);
+
 // 3-D FP16 tensor map over [64][rows][C] (C fastest), box {64, box_rows, 1},
 // SWIZZLE_128B: the layout of the UMMA K-major operands.
 bool tc_encode_operand_map(CUtensorMap* map, const void* ptr, int C, long long rows,

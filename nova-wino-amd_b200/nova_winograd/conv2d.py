@@ -102,6 +102,7 @@ class NovaWinogradFunction(torch.autograd.Function):
     def forward(ctx, input, weight, bias, padding, handle_holder):
         ctx.save_for_backward(input, weight, bias)
         ctx.padding = padding
+        ctx.weight_grad = getattr(handle_holder, "weight_grad", "fp32")
         x = input.half().contiguous() if input.dtype != torch.float16 else input.contiguous()
         return handle_holder._native_forward(x, bias)
 
@@ -114,7 +115,11 @@ class NovaWinogradFunction(torch.autograd.Function):
             grad_input = F.conv_transpose2d(go.float(), weight.float(),
                                             padding=ctx.padding).to(input.dtype)
         if ctx.needs_input_grad[1]:
-            grad_weight = _weight_grad(input, weight, go, ctx.padding).to(weight.dtype)
+            if ctx.weight_grad == "winograd" and input.shape[1] % 16 == 0:
+                from .ops import nova_weight_grad
+                grad_weight = nova_weight_grad(input.half(), go.half(), ctx.padding).to(weight.dtype)
+            else:
+                grad_weight = _weight_grad(input, weight, go, ctx.padding).to(weight.dtype)
         if bias is not None and ctx.needs_input_grad[2]:
             grad_bias = go.float().sum(dim=(0, 2, 3)).to(bias.dtype)
         return grad_input, grad_weight, grad_bias, None, None
@@ -287,7 +292,14 @@ class NovaWinogradConv2d(nn.Module):
 
 
 class NovaWinogradConv2dTrainable(NovaWinogradConv2d):
-    """NOVA conv with a backward pass: native forward, FP32 PyTorch backward."""
+    """NOVA conv with a backward pass: native forward, FP32 PyTorch backward.
+
+    ``weight_grad`` selects the weight gradient: "fp32" (default, as the
+    reference: exact FP32 convolution gradient) or "winograd" (the native NOVA
+    F(6,3) weight-gradient kernels, ops.nova_weight_grad; input channels a
+    multiple of 16, error of the order of the forward's)."""
+
+    weight_grad = "fp32"
 
     def forward(self, x):
         if not x.is_contiguous():

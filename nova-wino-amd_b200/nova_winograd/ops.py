@@ -60,6 +60,8 @@ SIGNATURES = {
     "nova_get_path": (c_int, [c_void_p]),
     "nova_device_status": (c_int, [c_void_p]),
     "nova_forward_noalloc": (c_int, [c_void_p, c_void_p, c_void_p] + [c_int] * 6 + [c_void_p]),
+    "nova_weight_grad_workspace_bytes": (c_longlong, [c_int] * 6),
+    "nova_weight_grad_v2": (c_int, [c_void_p] * 4 + [c_longlong] + [c_int] * 6 + [c_void_p]),
     "nova_version": (c_char_p, []),
 }
 
@@ -211,3 +213,30 @@ def nova_forward(input_fp16, weight_fp32, padding=1):
         finally:
             _lib.nova_destroy(handle)
     return output
+
+
+def nova_weight_grad(input_fp16, grad_output_fp16, padding=1):
+    """dL/dw of the 3x3 stride-1 convolution by the NOVA F(6,3) Winograd
+    algorithm on the GPU (the reference's FP32 unfold loop, conv2d.py:131-141,
+    replaced by native kernels): input [B, C, H, W] and grad_output
+    [B, K, H_out, W_out], both float16 CUDA tensors; returns float32
+    [K, C, 3, 3].  Requires C to be a multiple of 16; its error against the
+    exact gradient is of the order of the forward's (a few percent)."""
+    lib = get_lib()
+    if input_fp16.dtype != torch.float16 or grad_output_fp16.dtype != torch.float16:
+        raise TypeError("input and grad_output must be float16")
+    x = input_fp16.contiguous()
+    dy = grad_output_fp16.contiguous()
+    B, C, H, W = x.shape
+    K = dy.shape[1]
+    if not (x.is_cuda and dy.is_cuda and x.device == dy.device):
+        raise ValueError("input and grad_output must be CUDA tensors on one device")
+    with torch.cuda.device(x.device):
+        nbytes = lib.nova_weight_grad_workspace_bytes(B, C, K, H, W, padding)
+        if nbytes < 0:
+            raise ValueError("bad sizes for nova_weight_grad")
+        ws = torch.empty(nbytes, dtype=torch.uint8, device=x.device)
+        dw = torch.empty(K, C, 3, 3, dtype=torch.float32, device=x.device)
+        check(lib.nova_weight_grad_v2(ptr(x), ptr(dy), ptr(dw), ptr(ws), nbytes, B, C, K, H, W,
+                                      padding, stream_ptr()), "nova_weight_grad")
+    return dw

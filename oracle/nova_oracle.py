@@ -319,6 +319,45 @@ def within_fp32_reordering(a: np.ndarray, b: np.ndarray, scale: np.ndarray,
 
 
 # ---------------------------------------------------------------------------
+# Weight gradient by the same algorithm (checker for nova_weight_grad_v2).
+#
+# The reference's backward computes grad_weight exactly in FP32 with a
+# per-sample unfold loop (nova_winograd/conv2d.py:131-141).  Differentiating
+# the forward y = A [(G w G^T) . (B^T d B)] A^T with respect to w gives
+# dW = G^T [ sum over tiles (A^T dY A) . (B^T d B) ] G, the exact gradient in
+# exact arithmetic; "ref" stores both transforms in FP16 as the kernels do.
+# ---------------------------------------------------------------------------
+
+def weight_grad(x: np.ndarray, dy: np.ndarray, pad: int = 1, mode: str = "ref") -> np.ndarray:
+    """dW [K][C][3][3] (float32) from x [B][C][H][W] and dy [B][K][H_out][W_out]."""
+    A, _, G = matrices(mode)
+    Bn, C, H, W = x.shape
+    K = dy.shape[1]
+    nh, nw = live_tiling(H, W, pad)
+    H_out, W_out = H + 2 * pad - 2, W + 2 * pad - 2
+    V = input_transform(x, nh, nw, pad, mode)                  # [64][BP][C]
+    t = np.zeros((Bn, K, nh * 6, nw * 6), dtype=np.float32)
+    t[:, :, :H_out, :W_out] = dy.astype(np.float32)
+    t = t.reshape(Bn, K, nh, 6, nw, 6).transpose(0, 1, 2, 4, 3, 5)
+    g = A.T @ t @ A                                            # [B, K, nh, nw, 8, 8]
+    g = _round(g.transpose(4, 5, 0, 2, 3, 1).reshape(64, Bn * nh * nw, K), mode)
+    ug = np.einsum("pbk,pbc->pkc", g.astype(np.float64), V.astype(np.float64))
+    dw = np.einsum("nr,nmkc,ms->kcrs", G.astype(np.float64), ug.reshape(8, 8, K, C),
+                   G.astype(np.float64))
+    return dw.astype(np.float32)
+
+
+def direct_weight_grad_fp64(x: np.ndarray, dy: np.ndarray, pad: int = 1) -> np.ndarray:
+    """The exact weight gradient of the 3x3 stride-1 convolution, in FP64."""
+    Bn, C, H, W = x.shape
+    H_out, W_out = dy.shape[2], dy.shape[3]
+    xp = np.zeros((Bn, C, H + 2 * pad, W + 2 * pad), dtype=np.float64)
+    xp[:, :, pad:pad + H, pad:pad + W] = x.astype(np.float64)
+    win = np.lib.stride_tricks.sliding_window_view(xp, (3, 3), axis=(2, 3))[:, :, :H_out, :W_out]
+    return np.einsum("bkhw,bchwij->kcij", dy.astype(np.float64), win, optimize=True)
+
+
+# ---------------------------------------------------------------------------
 # FP64 direct convolution (the accuracy yardstick) and the error metric.
 # ---------------------------------------------------------------------------
 

@@ -209,3 +209,17 @@ def test_exact_order_restatement_agrees_with_fast_oracle():
     bad = ys.copy()
     bad[0, 0, 0, 0] = np.float16(float(bad[0, 0, 0, 0]) + 0.5)
     assert not o.within_fp32_reordering(bad, ys, np.zeros(ys.shape), 16).all()
+
+
+def test_weight_grad_identity():
+    """dW = G^T [sum over tiles (A^T dY A) . (B^T d B)] G is the exact weight
+    gradient: in the "exact" mode it matches the FP64 direct gradient (ragged
+    tiles and pad 0 included); with the FP16 storage of the transforms its error
+    is of the order of the forward's."""
+    rng = np.random.default_rng(1)
+    for (B, C, K, H, W, pad) in [(2, 16, 24, 13, 17, 1), (1, 8, 8, 10, 9, 0)]:
+        x = rng.standard_normal((B, C, H, W)).astype(np.float16)
+        dy = rng.standard_normal((B, K, H + 2 * pad - 2, W + 2 * pad - 2)).astype(np.float16)
+        d = o.direct_weight_grad_fp64(x, dy, pad)
+        assert o.rel_l2(o.weight_grad(x, dy, pad, "exact"), d) < 1e-4
+        assert o.rel_l2(o.weight_grad(x, dy, pad, "ref"), d) < 0.08
