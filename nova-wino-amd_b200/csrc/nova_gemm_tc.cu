@@ -45,7 +45,7 @@ constexpr int kSmemLimit = (227 * 1024) / kCtasPerSm - (kCtasPerSm > 1 ? 1024 : 
 
 struct Params {
   __half* M;
-  float* Mf;       // non-null: FP32 output, accumulated with atomic adds (split reduction)
+  float* Mf;       // non-null: FP32 output, one [64][BP][K] slice per split of the reduction
   long long BP;
   int C, K, BN;
   int n_bp_tiles, n_k_tiles, n_cblk;
@@ -287,15 +287,18 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
       }
       const long long bp = (long long)bpt * kBM + row;
       if (p.Mf) {
-        // FP32 partial sums of this tile's reduction range, added into the
-        // output (other splits of the same tile add theirs).
-        float* outf = p.Mf + ((long long)pos * p.BP + bp) * p.K + (long long)kt * p.BN;
+        // FP32 output: each split of the reduction writes its partial sums to
+        // its own slice (the caller adds the slices in a fixed order).
+        const long long split = cb0_ / p.kb_per_split;
+        float* outf = p.Mf + split * 64ll * p.BP * p.K + ((long long)pos * p.BP + bp) * p.K +
+                      (long long)kt * p.BN;
         for (int j = 0; j < p.BN; j += 16) {
           uint32_t r[16];
           tmem_ld16(taddr + j, r);
           if (bp < p.BP) {
 #pragma unroll
-            for (int q = 0; q < 16; ++q) atomicAdd(outf + j + q, __uint_as_float(r[q]));
+            for (int q = 0; q < 16; q += 4)
+              *reinterpret_cast<uint4*>(outf + j + q) = make_uint4(r[q], r[q + 1], r[q + 2], r[q + 3]);
           }
         }
         tc_fence_before();
@@ -531,6 +534,22 @@ static bool encode_pitched_map(CUtensorMap* map, const void* ptr, long long inne
             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+// Splits of the reduction: only when the output tiles alone would leave most
+// SMs idle; enough for about two tiles per SM, at least two 64-tile blocks of
+// reduction per split, at most kWgradMaxSplits.
+int tc_gemm_wgrad_splits(int K, int C, long long BP, int num_sms) {
+  const int BN = tc::pick_bn(C);
+  if (BN == 0) return 1;
+  const long long base = 64ll * ((K + tc::kBM - 1) / tc::kBM) * (C / BN);
+  if (2 * base >= num_sms) return 1;
+  const long long n_cblk = (BP + tc::kBK - 1) / tc::kBK;
+  long long n = std::min<long long>(n_cblk / 2, (2ll * num_sms + base - 1) / base);
+  n = std::min<long long>(n, kWgradMaxSplits);
+  if (n < 1) n = 1;
+  const long long per = (n_cblk + n - 1) / n;
+  return (int)((n_cblk + per - 1) / per);
+}
+
 cudaError_t tc_gemm_wgrad_run(const __half* A, const __half* Bop, float* Ug, int K, int C,
                               long long BP, long long pitch, int* dev_status, int num_sms,
                               cudaStream_t s, const char** why) {
@@ -561,10 +580,8 @@ cudaError_t tc_gemm_wgrad_run(const __half* A, const __half* Bop, float* Ug, int
   p.n_k_tiles = C / BN;
   p.n_cblk = (int)((BP + tc::kBK - 1) / tc::kBK);
   const long long base = 64ll * p.n_bp_tiles * p.n_k_tiles;
-  int n_split = (int)std::min<long long>(p.n_cblk, (2ll * num_sms + base - 1) / base);
-  if (n_split < 1) n_split = 1;
-  p.kb_per_split = (p.n_cblk + n_split - 1) / n_split;
-  p.n_split = (p.n_cblk + p.kb_per_split - 1) / p.kb_per_split;
+  p.n_split = tc_gemm_wgrad_splits(K, C, BP, num_sms);
+  p.kb_per_split = (p.n_cblk + p.n_split - 1) / p.n_split;
   p.total_tiles = base * p.n_split;
   p.tma_store = 0;
   p.status = dev_status;

@@ -129,9 +129,13 @@ bool tc2_gemm_eligible(const TcGemmPlan& plan, long long BP);
 cudaError_t tc2_gemm_run(const TcGemmPlan& plan, const __half* V, __half* M, long long BP,
                          int* dev_status, int num_sms, cudaStream_t s, const char** why);
 
-// Weight-gradient GEMM: Ug[pos][K][C] += sum_bp A[pos][K][bp] * Bop[pos][C][bp]
-// (rows `pitch` halves apart, bp < BP valid), FP32 atomic adds, reduction split
-// over CTAs.  Ug must be zeroed first.
+// Weight-gradient GEMM: Ug[pos][K][C] = sum_bp A[pos][K][bp] * Bop[pos][C][bp]
+// (rows `pitch` halves apart, bp < BP valid), FP32.  The reduction is split
+// over CTAs when the output tiles alone cannot fill the GPU: split s writes
+// its partial sums to Ug + s * 64 * K * C, and the caller adds the
+// tc_gemm_wgrad_splits() slices.
+constexpr int kWgradMaxSplits = 8;
+int tc_gemm_wgrad_splits(int K, int C, long long BP, int num_sms);
 cudaError_t tc_gemm_wgrad_run(const __half* A, const __half* Bop, float* Ug, int K, int C,
                               long long BP, long long pitch, int* dev_status, int num_sms,
                               cudaStream_t s, const char** why);

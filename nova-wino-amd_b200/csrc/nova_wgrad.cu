@@ -28,7 +28,14 @@
 namespace nova {
 namespace wgrad {
 
-constexpr int kChanPerWarp = 8;  // channels a warp walks for its 32 tiles
+constexpr int kChanPerBlock = 4;  // one channel per warp, the same 32 tiles
+
+// G for runtime-indexed rows (the same FP32 table as kG).
+__constant__ float c_G[8][3] = {
+    {kG(0, 0), kG(0, 1), kG(0, 2)}, {kG(1, 0), kG(1, 1), kG(1, 2)},
+    {kG(2, 0), kG(2, 1), kG(2, 2)}, {kG(3, 0), kG(3, 1), kG(3, 2)},
+    {kG(4, 0), kG(4, 1), kG(4, 2)}, {kG(5, 0), kG(5, 1), kG(5, 2)},
+    {kG(6, 0), kG(6, 1), kG(6, 2)}, {kG(7, 0), kG(7, 1), kG(7, 2)}};
 
 // m[n] = sum_i A[i][n] g[i]  (6 -> 8, the transpose of a_1d): the columns of A
 // pair up as n = 1/2, 3/4, 5/6 (even part +- odd part); n = 0 and 7 are g[0]
@@ -63,14 +70,14 @@ struct TArgs {
   long long BP, pitch;
 };
 
-// V^T[pos][c][bp] = (B^T d B)[pos] for tile bp, channel c.  Block: 4 warps of
-// 32 consecutive tiles; blockIdx.y picks kChanPerWarp channels.
-__global__ void __launch_bounds__(128, 4) input_transform_t(const __half* __restrict__ x,
+// V^T[pos][c][bp] = (B^T d B)[pos] for tile bp, channel c.  Block: 32
+// consecutive tiles (one per lane) x kChanPerBlock channels (one per warp).
+__global__ void __launch_bounds__(128) input_transform_t(const __half* __restrict__ x,
                                                          __half* __restrict__ VT, const TArgs a) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const long long bp = ((long long)blockIdx.x * 4 + warp) * 32 + lane;
-  const int c0 = blockIdx.y * kChanPerWarp;
-  if (bp >= a.BP) return;
+  const long long bp = (long long)blockIdx.x * 32 + lane;
+  const int c0 = blockIdx.y * kChanPerBlock + warp;
+  if (bp >= a.BP || c0 >= a.Cn) return;
   const int P = a.nh * a.nw;
   const int b = (int)(bp / P);
   const int tp = (int)(bp - (long long)b * P);
@@ -87,8 +94,8 @@ __global__ void __launch_bounds__(128, 4) input_transform_t(const __half* __rest
     const int w = w0 + i;
     if (w >= 0 && w < a.W) cmask |= 1u << i;
   }
-#pragma unroll 1
-  for (int c = c0; c < c0 + kChanPerWarp && c < a.Cn; ++c) {
+  {
+    const int c = c0;
     const __half* xc = x + ((long long)b * a.Cn + c) * plane + w0;
     // The window, packed in column pairs (32 registers).
     __half2 pr[8][4];
@@ -144,17 +151,17 @@ __global__ void __launch_bounds__(128, 4) grad_output_transform_t(const __half* 
                                                                __half* __restrict__ GT,
                                                                const TArgs a) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const long long bp = ((long long)blockIdx.x * 4 + warp) * 32 + lane;
-  const int k0 = blockIdx.y * kChanPerWarp;
-  if (bp >= a.BP) return;
+  const long long bp = (long long)blockIdx.x * 32 + lane;
+  const int k0 = blockIdx.y * kChanPerBlock + warp;
+  if (bp >= a.BP || k0 >= a.Cn) return;
   const int P = a.nh * a.nw;
   const int b = (int)(bp / P);
   const int tp = (int)(bp - (long long)b * P);
   const int th = tp / a.nw, tw = tp - th * a.nw;
   const int h0 = th * 6, w0 = tw * 6;
   const long long plane = (long long)a.H * a.W;
-#pragma unroll 1
-  for (int k = k0; k < k0 + kChanPerWarp && k < a.Cn; ++k) {
+  {
+    const int k = k0;
     const __half* gk = dy + ((long long)b * a.Cn + k) * plane;
     float tt[8][6];
 #pragma unroll
@@ -185,46 +192,65 @@ __global__ void __launch_bounds__(128, 4) grad_output_transform_t(const __half* 
   }
 }
 
-// dW[k][c][u][v] = sum_{n,m} G[n][u] G[m][v] Ug[n*8+m][k][c], FP32.
+// dW[k][c][u][v] = sum_{n,m} G[n][u] G[m][v] Ug[n*8+m][k][c], FP32.  Ug holds
+// n_split slices of partial sums over the tiles, added here in slice order.
+// Block: 32 consecutive (k, c) pairs (one per lane) x the 8 position rows n
+// (one per warp): warp n forms G[n][u] sum_m Ug[n][m] G[m][v] for its rows,
+// and the 8 partial 3x3 results are added through shared memory in n order.
 __global__ void __launch_bounds__(256) filter_back_transform(const float* __restrict__ Ug,
                                                              float* __restrict__ dw, int K,
-                                                             int C) {
-  const long long kc = (long long)blockIdx.x * blockDim.x + threadIdx.x;
-  if (kc >= (long long)K * C) return;
+                                                             int C, int n_split) {
+  __shared__ float part[8][9][33];
+  const int lane = threadIdx.x & 31, n = threadIdx.x >> 5;
   const long long stride = (long long)K * C;
-  float t[8][3];  // t[n][v] = sum_m Ug[n][m] G[m][v]
-#pragma unroll
-  for (int n = 0; n < 8; ++n) {
+  const long long kc = (long long)blockIdx.x * 32 + lane;
+  if (kc < stride) {
     float u[8];
 #pragma unroll
-    for (int m = 0; m < 8; ++m) u[m] = Ug[(n * 8 + m) * stride + kc];
+    for (int m = 0; m < 8; ++m) {
+      const float* q = Ug + (n * 8 + m) * stride + kc;
+      float acc = q[0];
+      for (int sp = 1; sp < n_split; ++sp) acc += q[(long long)sp * 64 * stride];
+      u[m] = acc;
+    }
 #pragma unroll
     for (int v = 0; v < 3; ++v) {
-      float acc = 0.f;
+      float t = 0.f;  // sum_m Ug[n][m] G[m][v]
 #pragma unroll
-      for (int m = 0; m < 8; ++m) acc = fmaf(u[m], kG(m, v), acc);
-      t[n][v] = acc;
+      for (int m = 0; m < 8; ++m) t = fmaf(u[m], kG(m, v), t);
+#pragma unroll
+      for (int uu = 0; uu < 3; ++uu) part[n][uu * 3 + v][lane] = c_G[n][uu] * t;
     }
   }
-  float* o = dw + kc * 9;
+  __syncthreads();
+  // 32 pairs x 9 outputs, one thread each (the first 288 of 256 threads loop).
+  for (int i = threadIdx.x; i < 32 * 9; i += blockDim.x) {
+    const int l = i / 9, e = i - (i / 9) * 9;
+    const long long kcl = (long long)blockIdx.x * 32 + l;
+    if (kcl >= stride) continue;
+    float acc = 0.f;
 #pragma unroll
-  for (int uu = 0; uu < 3; ++uu)
-#pragma unroll
-    for (int v = 0; v < 3; ++v) {
-      float acc = 0.f;
-#pragma unroll
-      for (int n = 0; n < 8; ++n) acc = fmaf(kG(n, uu), t[n][v], acc);
-      o[uu * 3 + v] = acc;
-    }
+    for (int nn = 0; nn < 8; ++nn) acc += part[nn][e][l];
+    dw[kcl * 9 + e] = acc;
+  }
 }
 
 struct Layout {
   int nh, nw, H_out, W_out;
   long long BP, pitch;
+  int splits;  // slices of partial sums the GEMM writes (device-dependent)
   size_t vt_bytes, gt_bytes, ug_bytes, total;  // total includes a 256-byte status word
 };
 
 static size_t align256(size_t b) { return (b + 255) & ~size_t(255); }
+
+static int device_sms() {
+  int dev = 0, sms = 148;
+  if (cudaGetDevice(&dev) == cudaSuccess &&
+      cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
+    sms = 148;
+  return sms;
+}
 
 static bool layout(int B, int C, int K, int H, int W, int pad, Layout* L) {
   if (B <= 0 || C <= 0 || K <= 0 || H <= 0 || W <= 0 || pad < 0) return false;
@@ -237,7 +263,8 @@ static bool layout(int B, int C, int K, int H, int W, int pad, Layout* L) {
   L->pitch = (L->BP + 7) / 8 * 8;  // 16-byte row pitch for the GEMM's tensor maps
   L->vt_bytes = align256((size_t)64 * C * L->pitch * 2);
   L->gt_bytes = align256((size_t)64 * K * L->pitch * 2);
-  L->ug_bytes = align256((size_t)64 * K * C * 4);
+  L->splits = tc_gemm_wgrad_splits(K, C, L->BP, device_sms());
+  L->ug_bytes = align256((size_t)L->splits * 64 * K * C * 4);
   L->total = L->vt_bytes + L->gt_bytes + L->ug_bytes + 256;
   return true;
 }
@@ -277,20 +304,18 @@ extern "C" __attribute__((visibility("default"))) int nova_weight_grad_v2(
   float* Ug = reinterpret_cast<float*>(ws + L.vt_bytes + L.gt_bytes);
   // The GEMM's bounded waits record an expiry here (never read by this call).
   int* status = reinterpret_cast<int*>(ws + L.vt_bytes + L.gt_bytes + L.ug_bytes);
-  int dev = 0, sms = 148;
-  if (cudaGetDevice(&dev) == cudaSuccess)
-    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-  cudaError_t e = cudaMemsetAsync(Ug, 0, L.ug_bytes + 256, s);
-  const unsigned gx = (unsigned)((L.BP + 127) / 128);
+  const int sms = device_sms();
+  cudaError_t e = cudaMemsetAsync(status, 0, 256, s);
+  const unsigned gx = (unsigned)((L.BP + 31) / 32);
   if (e == cudaSuccess) {
     TArgs ai{C, H, W, pad, L.nh, L.nw, L.BP, L.pitch};
-    input_transform_t<<<dim3(gx, (C + kChanPerWarp - 1) / kChanPerWarp), 128, 0, s>>>(
+    input_transform_t<<<dim3(gx, (C + kChanPerBlock - 1) / kChanPerBlock), 128, 0, s>>>(
         static_cast<const __half*>(d_input), VT, ai);
     e = cudaGetLastError();
   }
   if (e == cudaSuccess) {
     TArgs ag{K, L.H_out, L.W_out, 0, L.nh, L.nw, L.BP, L.pitch};
-    grad_output_transform_t<<<dim3(gx, (K + kChanPerWarp - 1) / kChanPerWarp), 128, 0, s>>>(
+    grad_output_transform_t<<<dim3(gx, (K + kChanPerBlock - 1) / kChanPerBlock), 128, 0, s>>>(
         static_cast<const __half*>(d_grad_output), GT, ag);
     e = cudaGetLastError();
   }
@@ -300,8 +325,8 @@ extern "C" __attribute__((visibility("default"))) int nova_weight_grad_v2(
   e = tc_gemm_wgrad_run(GT, VT, Ug, K, C, L.BP, L.pitch, status, sms, s, &why);
   if (e != cudaSuccess) return record_error(NOVA_ERR_CUDA, std::string("weight_grad: ") + why);
   const long long kc = (long long)K * C;
-  filter_back_transform<<<(unsigned)((kc + 255) / 256), 256, 0, s>>>(
-      Ug, static_cast<float*>(d_grad_weight), K, C);
+  filter_back_transform<<<(unsigned)((kc + 31) / 32), 256, 0, s>>>(
+      Ug, static_cast<float*>(d_grad_weight), K, C, L.splits);
   e = cudaGetLastError();
   if (e != cudaSuccess)
     return record_error(NOVA_ERR_CUDA, std::string("weight_grad: ") + cudaGetErrorString(e));
