@@ -379,18 +379,18 @@ def vendor_layer_times(layers, flush, reps=20):
 # the 126 MB L2 are missing here; the totals therefore sit below the algorithmic
 # bytes rather than above them (no kernel re-reads its input).
 NCU_DRAM_BYTES_B128 = {
-    "conv2_x": {"input_transform_kernel": (51408896, 52868608),
-                "gemm_tc_kernel": (105416192, 52318720),
-                "output_transform_kernel": (104876544, 16097280)},
-    "conv3_x": {"input_transform_kernel": (25714176, 788224),
-                "gemm_tc_kernel": (54556928, 4594432),
-                "output_transform_kernel": (52446464, 57344)},
-    "conv4_x": {"input_transform_kernel": (12876288, 6656),
-                "gemm_tc_kernel": (46167552, 53760),
-                "output_transform_kernel": (37768192, 0)},
-    "conv5_x": {"input_transform_kernel": (6447872, 16384),
-                "gemm_tc_kernel": (67140096, 997376),
-                "output_transform_kernel": (33570560, 0)},
+    "conv2_x": {"input_transform_kernel": (51412736, 43130112),
+                "gemm_tc_kernel": (105418496, 55179776),
+                "output_transform_kernel": (104874752, 16134656)},
+    "conv3_x": {"input_transform_kernel": (25713664, 752640),
+                "gemm_tc_kernel": (54562816, 3790848),
+                "output_transform_kernel": (52446464, 66560)},
+    "conv4_x": {"input_transform_kernel": (12875520, 0),
+                "gemm_tc_kernel": (46173952, 204544),
+                "output_transform_kernel": (37768448, 0)},
+    "conv5_x": {"input_transform_kernel": (6443264, 0),
+                "gemm_tc_kernel": (67145216, 401664),
+                "output_transform_kernel": (33572352, 0)},
 }
 
 
