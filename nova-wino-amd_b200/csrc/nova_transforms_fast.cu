@@ -539,7 +539,22 @@ __global__ void __launch_bounds__(32 * StreamGeo<TPC>::kWarps, 1)
       const int w0 = tw0 * 6 - a.pad;
       const int x0 = w0 >= 0 ? (w0 & ~7) : -((-w0 + 7) & ~7);
       const int d = w0 - x0;
-      if (!mbar_wait_bounded(tc::smem_u32(&full[sl]), ph)) break;
+      // Every warp of the group waits (bounded) for the landing, then the group
+      // agrees on the outcome through the named barrier, so after an expiry the
+      // whole group leaves together and no warp is left at a later barrier.
+      {
+        const uint32_t ok = mbar_wait_bounded(tc::smem_u32(&full[sl]), ph) ? 1u : 0u;
+        uint32_t all;
+        asm volatile(
+            "{\n\t.reg .pred p, q;\n\t"
+            "setp.ne.u32 p, %1, 0;\n\t"
+            "bar.red.and.pred q, %2, %3, p;\n\t"
+            "selp.u32 %0, 1, 0, q;\n\t}"
+            : "=r"(all)
+            : "r"(ok), "r"(named), "r"(32 * TPC)
+            : "memory");
+        if (!all) break;
+      }
       // Transpose the landing [channel][row][col] into [col][channel slot][row]
       // (as in input_transform_fast, mode 1), 8-column chunks over the group.
       constexpr int kChunks = Gm::kBoxW / 8;
