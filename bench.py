@@ -731,8 +731,7 @@ def run_nova(args):
     ms_per_step = total_ms / args.steps
     value = world * flops_step * args.steps / (total_ms / 1e3) / 1e12
     from nova_winograd import ops
-    windows = 1
-    launches = 3 * len(LAYERS) * args.steps * windows
+    launches = 3 * len(LAYERS) * args.steps  # input transform, GEMM, output transform
 
     # End to end through the public module API: pinned host input -> device,
     # forward, output -> pinned host, every step.
