@@ -200,33 +200,54 @@ __global__ void __launch_bounds__(128, 4) grad_output_transform_t(const __half* 
 __global__ void __launch_bounds__(256) filter_back_transform(const float* __restrict__ Ug,
                                                              float* __restrict__ dw, int K,
                                                              int C, int n_split) {
-  __shared__ float part[8][9][33];
+  // Block: 128 consecutive (k, c) pairs, four per lane (16-byte loads; K * C is
+  // a multiple of 4 since C is a multiple of 16), x the 8 position rows n (one
+  // per warp).
+  __shared__ float part[8][9][132];
   const int lane = threadIdx.x & 31, n = threadIdx.x >> 5;
   const long long stride = (long long)K * C;
-  const long long kc = (long long)blockIdx.x * 32 + lane;
-  if (kc < stride) {
-    float u[8];
+  const long long kc0 = (long long)blockIdx.x * 128 + lane * 4;
+  if (kc0 < stride) {
+    float4 u[8];
 #pragma unroll
     for (int m = 0; m < 8; ++m) {
-      const float* q = Ug + (n * 8 + m) * stride + kc;
-      float acc = q[0];
-      for (int sp = 1; sp < n_split; ++sp) acc += q[(long long)sp * 64 * stride];
+      const float* q = Ug + (n * 8 + m) * stride + kc0;
+      float4 acc = *reinterpret_cast<const float4*>(q);
+      for (int sp = 1; sp < n_split; ++sp) {
+        const float4 t = *reinterpret_cast<const float4*>(q + (long long)sp * 64 * stride);
+        acc.x += t.x;
+        acc.y += t.y;
+        acc.z += t.z;
+        acc.w += t.w;
+      }
       u[m] = acc;
     }
 #pragma unroll
     for (int v = 0; v < 3; ++v) {
-      float t = 0.f;  // sum_m Ug[n][m] G[m][v]
+      float4 t = make_float4(0.f, 0.f, 0.f, 0.f);  // sum_m Ug[n][m] G[m][v]
 #pragma unroll
-      for (int m = 0; m < 8; ++m) t = fmaf(u[m], kG(m, v), t);
+      for (int m = 0; m < 8; ++m) {
+        t.x = fmaf(u[m].x, kG(m, v), t.x);
+        t.y = fmaf(u[m].y, kG(m, v), t.y);
+        t.z = fmaf(u[m].z, kG(m, v), t.z);
+        t.w = fmaf(u[m].w, kG(m, v), t.w);
+      }
 #pragma unroll
-      for (int uu = 0; uu < 3; ++uu) part[n][uu * 3 + v][lane] = c_G[n][uu] * t;
+      for (int uu = 0; uu < 3; ++uu) {
+        const float g = c_G[n][uu];
+        float* dst = &part[n][uu * 3 + v][lane * 4];
+        dst[0] = g * t.x;
+        dst[1] = g * t.y;
+        dst[2] = g * t.z;
+        dst[3] = g * t.w;
+      }
     }
   }
   __syncthreads();
-  // 32 pairs x 9 outputs, one thread each (the first 288 of 256 threads loop).
-  for (int i = threadIdx.x; i < 32 * 9; i += blockDim.x) {
+  // 128 pairs x 9 outputs: consecutive threads write consecutive floats of dW.
+  for (int i = threadIdx.x; i < 128 * 9; i += blockDim.x) {
     const int l = i / 9, e = i - (i / 9) * 9;
-    const long long kcl = (long long)blockIdx.x * 32 + l;
+    const long long kcl = (long long)blockIdx.x * 128 + l;
     if (kcl >= stride) continue;
     float acc = 0.f;
 #pragma unroll
@@ -325,7 +346,7 @@ extern "C" __attribute__((visibility("default"))) int nova_weight_grad_v2(
   e = tc_gemm_wgrad_run(GT, VT, Ug, K, C, L.BP, L.pitch, status, sms, s, &why);
   if (e != cudaSuccess) return record_error(NOVA_ERR_CUDA, std::string("weight_grad: ") + why);
   const long long kc = (long long)K * C;
-  filter_back_transform<<<(unsigned)((kc + 31) / 32), 256, 0, s>>>(
+  filter_back_transform<<<(unsigned)((kc + 127) / 128), 256, 0, s>>>(
       Ug, static_cast<float*>(d_grad_weight), K, C, L.splits);
   e = cudaGetLastError();
   if (e != cudaSuccess)
