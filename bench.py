@@ -953,6 +953,18 @@ def resnet50_measure(batch, steps, warmup, device, dist, world, rank):
         "gpu_launches": 3 * n_rep * steps,
     }
     if rank == 0:
+        # Batch 1 (config 3's latency case): eager forwards, and the whole
+        # network captured once in a CUDA graph and replayed (the module's
+        # forward is capturable), NOVA and cuDNN.
+        x1 = x[:1].clone()
+        b1 = {}
+        for label, m in (("nova", model), ("cudnn", ref)):
+            with torch.no_grad():
+                b1[label + "_eager_ms"] = round(back_to_back_us(lambda: m(x1), reps=50) / 1e3, 4)
+                g = graph_of(lambda: m(x1))
+                b1[label + "_graph_ms"] = round(back_to_back_us(g.replay, reps=50) / 1e3, 4)
+                del g
+        rec["batch1"] = b1
         # Every replaced conv's output for image 0, from the activations the
         # model feeds it, against the oracle (hooks outside the timed region).
         seen = []
@@ -1002,6 +1014,7 @@ def run_resnet50(args):
             "logits_finite": rec["logits_finite"],
             "logits_rel_diff_vs_cudnn": rec["logits_rel_diff_vs_cudnn"],
             "conv_parity_image0": rec.get("conv_parity_image0"),
+            "batch1": rec.get("batch1"),
             "clocks": clocks,
         })
     if dist is not None:
