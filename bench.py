@@ -491,9 +491,6 @@ class _TorchCuda:
     def use(self, stream):
         return self.torch.cuda.stream(stream)
 
-    def keep_alive(self, tensor, stream):
-        tensor.record_stream(stream)
-
     def synchronize(self):
         self.torch.cuda.synchronize()
 
@@ -504,13 +501,18 @@ def e2e_pipelined(hx, dx, hy, forwards, steps, cu, before_timing=None):
     to pinned host memory.  Host-to-device copies run on one stream and
     device-to-host copies on another, so layer i + 1's input crosses PCIe while
     layer i computes and layer i - 1's output returns.  A device input buffer
-    is refilled only after the forward that read it, and each output is kept
-    alive on the copy-out stream until its copy ends.  Returns the elapsed ms
+    is refilled only after the forward that read it.  Each output is held by
+    reference until the next step's forward of the same layer, and that forward
+    first waits (on the compute stream) for the output's copy out: only then is
+    the old output released, so the allocator can hand its memory to later
+    compute-stream work only after the copy has read it.  Returns the elapsed ms
     of the ``steps`` steps (CUDA events on the compute stream, which waits for
     the last copy out)."""
     comp = cu.current()
     s_in, s_out = cu.stream(), cu.stream()
     consumed = [None] * len(hx)
+    copied = [None] * len(hx)
+    held = [None] * len(hx)
     start, end = cu.event(True), cu.event(True)
     if before_timing is not None:
         before_timing()
@@ -525,14 +527,20 @@ def e2e_pipelined(hx, dx, hy, forwards, steps, cu, before_timing=None):
                 landed = cu.event()
                 landed.record(s_in)
             comp.wait_event(landed)
+            if copied[i] is not None:
+                comp.wait_event(copied[i])
+                held[i] = None  # its copy out is ordered before all later compute work
             y = fwd(dx[i])
+            held[i] = y
             done = cu.event()
             done.record(comp)
             consumed[i] = done
             with cu.use(s_out):
                 s_out.wait_event(done)
-                cu.keep_alive(y, s_out)
                 hy[i].copy_(y, non_blocking=True)
+                out_ev = cu.event()
+                out_ev.record(s_out)
+                copied[i] = out_ev
     last = cu.event()
     last.record(s_out)
     comp.wait_event(last)

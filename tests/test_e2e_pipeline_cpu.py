@@ -1,8 +1,8 @@
 """bench.e2e_pipelined on CPU with fake streams and events: every step copies
 each layer's input in, runs the layer and copies its output out; a device
-input buffer is refilled only after the forward that read it; every output is
-kept alive on the copy-out stream; the compute stream waits for the last copy
-out before the end event."""
+input buffer is refilled only after the forward that read it; each layer's next
+forward waits for the previous output's copy out; the compute stream waits for
+the last copy out before the end event."""
 
 import contextlib
 import os
@@ -67,9 +67,6 @@ class FakeCuda:
         finally:
             self.active.pop()
 
-    def keep_alive(self, tensor, stream):
-        self.kept.append((tensor, stream))
-
     def synchronize(self):
         pass
 
@@ -96,21 +93,21 @@ def test_pipelined_e2e_outputs_and_ordering():
         assert torch.equal(hy[k], hx[k] * (k + 2) + 1)
     assert calls == [0, 1, 2] * steps
     s_in, s_out = cu.made
-    # Every output stays alive on the copy-out stream.
-    assert len(cu.kept) == 3 * steps and all(s is s_out for _, s in cu.kept)
     # The copy-in stream starts after the start event, then waits, for every
     # refill after the first step, on the forward that read the buffer.
     waits_in = [e for op, e in s_in.log if op == "wait"]
     assert len(waits_in) == 1 + 3 * (steps - 1)
     assert all(e.stream is cu.comp for e in waits_in)
-    # Each copy out waits for its forward; compute waits for each landed input
+    # Each copy out waits for its forward; compute waits for each landed input,
+    # for the previous copy out of the same layer before every later forward,
     # and, at the end, for the last copy out.
     waits_out = [e for op, e in s_out.log if op == "wait"]
     assert len(waits_out) == 3 * steps and all(e.stream is cu.comp for e in waits_out)
     waits_comp = [e for op, e in cu.comp.log if op == "wait"]
-    assert len(waits_comp) == 3 * steps + 1
+    assert len(waits_comp) == 3 * steps + 3 * (steps - 1) + 1
     assert waits_comp[-1].stream is s_out
-    assert all(e.stream is s_in for e in waits_comp[:-1])
+    assert sum(e.stream is s_in for e in waits_comp) == 3 * steps
+    assert sum(e.stream is s_out for e in waits_comp) == 3 * (steps - 1) + 1
 
 
 def test_e2e_report_never_slower_than_serial():
