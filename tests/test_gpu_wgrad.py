@@ -28,6 +28,8 @@ CASES = [  # B, C, K, H, W, pad
     (4, 256, 256, 14, 14, 1),
     (2, 512, 512, 7, 7, 1),
     (8, 64, 64, 56, 56, 1),
+    (3, 16, 8, 1, 1, 1),      # single pixel: one tile, almost all padding
+    (2, 48, 5, 9, 7, 2),      # pad 2, K not a multiple of 16
 ]
 
 
