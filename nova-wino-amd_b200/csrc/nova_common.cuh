@@ -191,6 +191,80 @@ __device__ __forceinline__ void bt_1d2_b(const float2 v[8], float2 f[4]) {
   f[3] = sub2(e3, o3);
 }
 
+// ---- Butterflies over inputs known to be zero ------------------------------
+// A tile whose window reaches past the image's last row (or column) has
+// inputs v[i] = 0 for i >= N.  Zv carries a value with a flag that is a
+// compile-time constant once the butterfly is unrolled; a term whose input is
+// known zero is dropped (fma(k, 0, c) == c), and an FMA onto a known-zero
+// accumulator becomes a multiply (fma(k, a, 0) == k * a, one rounding both
+// ways).  The remaining operations run in bt_1d2's order, so every output
+// equals bt_1d2's except possibly in the sign of an exact zero.
+struct Zv {
+  float2 v;
+  bool on;  // false: the value is known to be zero
+};
+__device__ __forceinline__ Zv zin(const float2* v, int i, int n) {
+  return i < n ? Zv{v[i], true} : Zv{make_float2(0.f, 0.f), false};
+}
+__device__ __forceinline__ Zv zmul(float k, Zv a) { return a.on ? Zv{mul2(k, a.v), true} : a; }
+__device__ __forceinline__ Zv zfma(float k, Zv a, Zv c) {
+  if (!a.on) return c;
+  if (!c.on) return Zv{mul2(k, a.v), true};
+  return Zv{fma2(k, a.v, c.v), true};
+}
+__device__ __forceinline__ float2 zadd(Zv a, Zv b) {
+  if (!a.on) return b.on ? b.v : make_float2(0.f, 0.f);
+  if (!b.on) return a.v;
+  return add2(a.v, b.v);
+}
+__device__ __forceinline__ float2 zsub(Zv a, Zv b) {
+  if (!b.on) return a.on ? a.v : make_float2(0.f, 0.f);
+  if (!a.on) return make_float2(-b.v.x, -b.v.y);
+  return sub2(a.v, b.v);
+}
+__device__ __forceinline__ float2 zval(Zv a) { return a.on ? a.v : make_float2(0.f, 0.f); }
+
+// bt_1d2 / bt_1d2_a / bt_1d2_b with v[i] = 0 for i >= N (N = 8: the same
+// operations as the dense forms).
+template <int N>
+__device__ __forceinline__ void bt_1d2_za(const float2 v[8], float2 f[4]) {
+  const Zv v0 = zin(v, 0, N), v1 = zin(v, 1, N), v2 = zin(v, 2, N), v3 = zin(v, 3, N);
+  const Zv v4 = zin(v, 4, N), v5 = zin(v, 5, N), v6 = zin(v, 6, N), v7 = zin(v, 7, N);
+  const Zv e1 = zfma(kB1361, v2, zfma(-kB2361, v4, v6));
+  const Zv o1 = zfma(kB0817, v1, zfma(-kB1417, v3, zmul(kB06, v5)));
+  f[0] = zval(zfma(-kB049, v0, zfma(kB2211, v2, zfma(-kB2721, v4, v6))));
+  f[1] = zadd(e1, o1);
+  f[2] = zsub(e1, o1);
+  f[3] = zval(zfma(-kB049, v1, zfma(kB2211, v3, zfma(-kB2721, v5, v7))));
+}
+template <int N>
+__device__ __forceinline__ void bt_1d2_zb(const float2 v[8], float2 f[4]) {
+  const Zv v1 = zin(v, 1, N), v2 = zin(v, 2, N), v3 = zin(v, 3, N);
+  const Zv v4 = zin(v, 4, N), v5 = zin(v, 5, N), v6 = zin(v, 6, N);
+  const Zv e2 = zfma(kB049, v2, zfma(-kB1721, v4, v6));
+  const Zv o2 = zfma(kB049, v1, zfma(-kB1721, v3, v5));
+  const Zv e3 = zfma(kB036, v2, zfma(-kB1360, v4, v6));
+  const Zv o3 = zfma(kB042, v1, zfma(-kB1587, v3, zmul(kB1167, v5)));
+  f[0] = zadd(e2, o2);
+  f[1] = zsub(e2, o2);
+  f[2] = zadd(e3, o3);
+  f[3] = zsub(e3, o3);
+}
+template <int N>
+__device__ __forceinline__ void bt_1d2_z(const float2 v[8], float2 f[8]) {
+  float2 a[4], b[4];
+  bt_1d2_za<N>(v, a);
+  bt_1d2_zb<N>(v, b);
+  f[0] = a[0];
+  f[1] = a[1];
+  f[2] = a[2];
+  f[3] = b[0];
+  f[4] = b[1];
+  f[5] = b[2];
+  f[6] = b[3];
+  f[7] = a[3];
+}
+
 __device__ __forceinline__ void a_1d2(const float2 m[8], float2 g[6]) {
   const float2 sa = add2(m[1], m[2]), da = sub2(m[1], m[2]);
   const float2 sb = add2(m[3], m[4]), db = sub2(m[3], m[4]);

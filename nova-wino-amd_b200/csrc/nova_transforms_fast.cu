@@ -868,6 +868,52 @@ constexpr int plane_it_min_blocks() {
   return n < 1 ? 1 : n;
 }
 
+// One tile of the plane input transform for the lane's channel pair: rows
+// (columns) of the 8 x 8 window at index >= NR (NC) are known zero, so their
+// loads and terms are skipped.  The column pass runs in two halves of its
+// output rows ({0,1,2,7}, {3,4,5,6}): 64 live registers for the intermediate
+// instead of 128 (no spills).
+template <class Pg, int NR, int NC>
+__device__ __forceinline__ void it_plane_tile(const __half* tile_s, __half2* const vt,
+                                              const long long step) {
+#pragma unroll 1
+  for (int half = 0; half < 2; ++half) {
+    float2 tt[4][8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      if (j >= NC) {
+#pragma unroll
+        for (int i = 0; i < 4; ++i) tt[i][j] = make_float2(0.f, 0.f);
+        continue;
+      }
+      float2 v[8], f[4];
+#pragma unroll
+      for (int i = 0; i < 8; ++i)
+        v[i] = i < NR ? __half22float2(*reinterpret_cast<const __half2*>(
+                            tile_s + (i * Pg::kCols + j) * Pg::kPitch))
+                      : make_float2(0.f, 0.f);
+      if (half == 0)
+        bt_1d2_za<NR>(v, f);
+      else
+        bt_1d2_zb<NR>(v, f);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) tt[i][j] = f[i];
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int r = half == 0 ? (i < 3 ? i : 7) : 3 + i;
+      float2 f[8];
+      bt_1d2_z<NC>(tt[i], f);
+      __half2* out = vt + (long long)(r * 8) * step;
+#pragma unroll
+      for (int s = 0; s < 8; ++s) {
+        st_global_h2(out, __float22half2_rn(f[s]));
+        out += step;
+      }
+    }
+  }
+}
+
 template <int TR, int TC, int kW, int kLand>
 __global__ void __launch_bounds__(32 * PlaneGeo<TR, TC, kW>::kWarps,
                                   (plane_it_min_blocks<TR, TC, kW, kLand>()))
@@ -1041,37 +1087,20 @@ __global__ void __launch_bounds__(32 * PlaneGeo<TR, TC, kW>::kWarps,
     __half2* const vt = reinterpret_cast<__half2*>(V + bp * C + c);
     const long long step = plane >> 1;  // one position plane of V, in half2
     const __half* tile_s = xs + ((tr * 6) * Pg::kCols + tc * 6) * Pg::kPitch + cl;
-    // Column pass in two halves of its output rows ({0,1,2,7}, {3,4,5,6}):
-    // 64 live registers for the intermediate instead of 128 (no spills).
-#pragma unroll 1
-    for (int half = 0; half < 2; ++half) {
-      float2 tt[4][8];
-#pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        float2 v[8], f[4];
-#pragma unroll
-        for (int i = 0; i < 8; ++i)
-          v[i] = __half22float2(
-              *reinterpret_cast<const __half2*>(tile_s + (i * Pg::kCols + j) * Pg::kPitch));
-        if (half == 0)
-          bt_1d2_a(v, f);
-        else
-          bt_1d2_b(v, f);
-#pragma unroll
-        for (int i = 0; i < 4; ++i) tt[i][j] = f[i];
-      }
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const int r = half == 0 ? (i < 3 ? i : 7) : 3 + i;
-        float2 f[8];
-        bt_1d2(tt[i], f);
-        __half2* out = vt + (long long)(r * 8) * step;
-#pragma unroll
-        for (int s = 0; s < 8; ++s) {
-          st_global_h2(out, __float22half2_rn(f[s]));
-          out += step;
-        }
-      }
+    // Window rows (columns) at or past H + pad (W + pad) lie in the zero
+    // border: a tile with at most 3 image rows (columns) takes the body that
+    // drops their terms.
+    const bool short_r = H + pad - 6 * tr <= 3, short_c = W + pad - 6 * tc <= 3;
+    if (short_r) {
+      if (short_c)
+        it_plane_tile<Pg, 3, 3>(tile_s, vt, step);
+      else
+        it_plane_tile<Pg, 3, 8>(tile_s, vt, step);
+    } else {
+      if (short_c)
+        it_plane_tile<Pg, 8, 3>(tile_s, vt, step);
+      else
+        it_plane_tile<Pg, 8, 8>(tile_s, vt, step);
     }
   }
   __syncthreads();
