@@ -692,7 +692,15 @@ def gemm_stage_b256(device, flush, peaks, reps=20):
         ms = time_kernel(gm, reps, flush)
         flops = 2.0 * 64 * C * C * BP
         tf = flops / ms / 1e9
+        # Calibration, not a product path: cuBLAS (torch.bmm, FP16 in and out)
+        # on the same 64 GEMMs of [BP, C] x [C, K], timed the same way.
+        Ut = torch.randn(64, C, C, dtype=torch.float16, device=device).transpose(1, 2)
+        Mc = torch.empty_like(M)
+        ms_cb = time_kernel(lambda: torch.bmm(V, Ut, out=Mc), reps, flush)
+        del Ut, Mc
         out[name] = {"gemm_us": round(ms * 1e3, 2), "tflops": round(tf, 1),
+                     "cublas_bmm_us": round(ms_cb * 1e3, 2),
+                     "cublas_bmm_tflops": round(flops / ms_cb / 1e9, 1),
                      "frac_of_peak": round(tf / peaks["bf16_tflops"], 4),
                      "peak": peaks["bf16_tflops"], "peak_kind": "dense bf16 burst (" +
                      peaks["source"] + ")",
@@ -1125,6 +1133,85 @@ def run_unet_model(args):
         dist.destroy_process_group()
 
 
+def gemm_trace(args):
+    """Wait breakdown of the tcgen05 GEMM's warp roles (library built with
+    -DNOVA_GEMM_TRACE, which adds SM-clock counters around every mbarrier
+    wait): per CTA, cycles the producer waits for a free stage, the MMA issuer
+    for a drained accumulator and for landed operands, the epilogue
+    warpgroups for a finished accumulator and for their slab's previous TMA
+    store; and the CTA's whole time.  Printed as microseconds at the clock
+    given by --trace-mhz, averaged over the CTAs and --steps launches, for
+    conv4_x and conv5_x at batch 128 and 256, L2 flushed before each launch
+    and warm."""
+    import ctypes
+    import numpy as np
+    import torch
+    from nova_winograd import ops
+    lib = ops.get_lib()
+    try:
+        tr = lib.nova_debug_gemm_trace
+    except AttributeError:
+        raise SystemExit("gemm-trace: the library was built without -DNOVA_GEMM_TRACE")
+    tr.restype = ctypes.c_int
+    tr.argtypes = [ctypes.c_void_p, ctypes.c_int]
+    device = torch.device("cuda", 0)
+    torch.cuda.set_device(device)
+    flush = make_flush(device)
+    buf = np.zeros((1024, 8), dtype=np.uint64)
+    cols = ["producer_wait_free_stage", "mma_wait_accumulator_drained", "mma_wait_operands",
+            "epilogue0_wait_accumulator", "epilogue1_wait_accumulator",
+            "epilogue0_wait_slab_store_read", "cta_total"]
+    nsm = torch.cuda.get_device_properties(device).multi_processor_count
+    out = {"unit": f"us at {args.trace_mhz} MHz (SM-clock cycles / MHz)"}
+    for B in (128, 256):
+        shapes = [l for l in LAYERS if l[0] in ("conv4_x", "conv5_x")]
+        for name, C, H, conv, x in build_layers(B, device, shapes):
+            nt = live_tiles(H)
+            BP = B * nt * nt
+            with torch.no_grad():
+                conv(x)
+            V = torch.empty(64, BP, C, dtype=torch.float16, device=device)
+            M = torch.empty_like(V)
+            s = ops.stream_ptr()
+            ops.check(lib.nova_input_transform_v2(ops.ptr(x), ops.ptr(V), B, C, H, H, 1, nt, nt,
+                                                  BP, s), "input_transform")
+            h = conv._handle
+
+            def gm():
+                ops.check(lib.nova_batched_gemm_v2(h, ops.ptr(V), ops.ptr(M), BP, s), "gemm")
+
+            for mode in ("flushed", "warm"):
+                gm()
+                torch.cuda.synchronize()
+                tr(None, 1)
+                torch.cuda.synchronize()
+                for _ in range(args.steps):
+                    if mode == "flushed":
+                        flush()
+                    gm()
+                torch.cuda.synchronize()
+                tr(buf.ctypes.data, 0)
+                cyc = buf[:nsm].astype(np.float64).mean(axis=0) / args.steps
+                rec = {c: round(float(v) / args.trace_mhz, 2) for c, v in zip(cols, cyc)}
+                # Event-timed duration of the same launches; CTA cycles over it
+                # bound the SM clock the kernel ran at from below.
+                if mode == "flushed":
+                    us = time_kernel(gm, args.steps, flush) * 1e3
+                else:
+                    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                    ev0.record()
+                    for _ in range(args.steps):
+                        gm()
+                    ev1.record()
+                    torch.cuda.synchronize()
+                    us = ev0.elapsed_time(ev1) * 1e3 / args.steps
+                rec["kernel_us_events"] = round(us, 2)
+                rec["sm_mhz_lower_bound"] = round(float(cyc[len(cols) - 1]) / us, 0)
+                out[f"{name}_B{B}_{mode}"] = rec
+            del V, M, x
+    print(json.dumps(out))
+
+
 def profile_stages(args):
     """Launch order: input transform, GEMM, output transform, repeated --steps
     times, for one sweep layer at --batch (reference counterpart:
@@ -1201,6 +1288,10 @@ def main():
                          "3x3 conv shapes one layer at a time against cuDNN")
     ap.add_argument("--fused", action="store_true",
                     help="with --profile-stages: run the fused single kernel instead (C, K <= 64)")
+    ap.add_argument("--gemm-trace", action="store_true",
+                    help="wait breakdown of the GEMM's warp roles (library built with "
+                         "-DNOVA_GEMM_TRACE)")
+    ap.add_argument("--trace-mhz", type=float, default=1965.0)
     ap.add_argument("--profile-stages", metavar="LAYER", default=None,
                     help="only run the three stage entries of one sweep layer (--steps times "
                          "each, no timing output): the driver for ncu captures")
@@ -1209,6 +1300,9 @@ def main():
         args.batch = 128 if args.workload in ("sweep", "resnet50") else 8
     if args.profile_stages:
         profile_stages(args)
+        return
+    if args.gemm_trace:
+        gemm_trace(args)
         return
     if args.impl == "reference":
         run_reference(args)

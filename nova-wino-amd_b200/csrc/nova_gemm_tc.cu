@@ -43,6 +43,15 @@ constexpr int kMaxBN = kTmemCols / 2 > 256 ? 256 : kTmemCols / 2;  // 2 accumula
 constexpr int kSlabCols = 64;   // epilogue staging: output columns per slab fill
 constexpr int kSmemLimit = (227 * 1024) / kCtasPerSm - (kCtasPerSm > 1 ? 1024 : 0);
 
+#ifdef NOVA_GEMM_TRACE
+__device__ unsigned long long g_gemm_trace[1024][8];
+#define TR_T0(v) const long long v = clock64()
+#define TR_ADD(slot, t0) atomicAdd(&g_gemm_trace[blockIdx.x & 1023][slot], (unsigned long long)(clock64() - (t0)))
+#else
+#define TR_T0(v)
+#define TR_ADD(slot, t0)
+#endif
+
 struct Params {
   __half* M;
   float* Mf;       // non-null: FP32 output, one [64][BP][K] slice per split of the reduction
@@ -139,6 +148,7 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
   pdl_wait();  // V (and U) come from earlier kernels in the stream
+  TR_T0(tk0);
 
   if (warp == 0) {
     if (lane == 0) {
@@ -151,10 +161,12 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
         int pos, bpt, kt, cb0, cb1;
         tile_of(p, t, pos, bpt, kt, cb0, cb1);
         for (int cb = cb0; cb < cb1; ++cb) {
+          TR_T0(tw0);
           if (!mbar_wait(smem_u32(&empty[s]), ph ^ 1u, abort_flag, p.status, kDevTimeoutProducer)) {
             ok = false;
             break;
           }
+          TR_ADD(0, tw0);
           const uint32_t sa = smem_u32(base + (size_t)s * stage_bytes);
           const uint32_t fb = smem_u32(&full[s]);
           mbar_expect_tx(fb, stage_bytes);
@@ -193,17 +205,21 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
       for (long long t = blockIdx.x; t < p.total_tiles && ok; t += gridDim.x, ++it) {
         const uint32_t acc = it & 1u;
         const uint32_t aph = (it >> 1) & 1u;
+        TR_T0(tw1);
         if (!mbar_wait(smem_u32(&tempty[acc]), aph ^ 1u, abort_flag, p.status, kDevTimeoutMma))
           break;
+        TR_ADD(1, tw1);
         tc_fence_after();
         const uint32_t dcol = tmem_base + acc * (uint32_t)p.BN;
         int pos_, bpt_, kt_, cb0, cb1;
         tile_of(p, t, pos_, bpt_, kt_, cb0, cb1);
         for (int cb = cb0; cb < cb1; ++cb) {
+          TR_T0(tw2);
           if (!mbar_wait(smem_u32(&full[s]), ph, abort_flag, p.status, kDevTimeoutMma)) {
             ok = false;
             break;
           }
+          TR_ADD(2, tw2);
           tc_fence_after();
           const uint32_t sa = smem_u32(base + (size_t)s * stage_bytes);
           const uint64_t ad = smem_desc_sw128(sa);
@@ -243,7 +259,9 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
       tile_of(p, t, pos, bpt, kt, cb0_, cb1_);
       const uint32_t acc = it & 1u;
       const uint32_t aph = (it >> 1) & 1u;
+      TR_T0(tw3);
       if (!mbar_wait(smem_u32(&tfull[acc]), aph, abort_flag, p.status, kDevTimeoutEpilogue)) break;
+      if (q == 0 && lane == 0) TR_ADD(3 + eg, tw3);
       tc_fence_after();
       const uint32_t taddr = tmem_base + ((uint32_t)(q * 32) << 16) + acc * (uint32_t)p.BN;
       if (p.tma_store) {
@@ -253,8 +271,10 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
         uint8_t* my_row = slab + lane * 128;
         for (int h0 = 0; h0 < p.BN; h0 += kSlabCols) {
           const int h1 = min(p.BN, h0 + kSlabCols);
+          TR_T0(tw5);
           if (lane == 0) bulk_wait_read_all();  // earlier stores have read the slab
           __syncwarp();
+          if (q == 0 && lane == 0 && eg == 0) TR_ADD(5, tw5);
           for (int j = h0; j < h1; j += 32) {
             uint32_t r[32];
             tmem_ld32(taddr + j, r);
@@ -329,6 +349,7 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
 
   tc_fence_before();
   __syncthreads();
+  if (threadIdx.x == 0) TR_ADD(6, tk0);
   pdl_trigger();  // after the whole CTA, epilogue stores included, is done
   if (warp == 1) {
     tc_fence_after();
@@ -609,4 +630,13 @@ cudaError_t tc_gemm_wgrad_run(const __half* A, const __half* Bop, float* Ug, int
   return e;
 }
 
+#ifdef NOVA_GEMM_TRACE
+extern "C" __attribute__((visibility("default"))) int nova_debug_gemm_trace(unsigned long long* out, int reset) {
+  if (reset) {
+    static unsigned long long z[1024][8];
+    return (int)cudaMemcpyToSymbol(tc::g_gemm_trace, z, sizeof(z));
+  }
+  return (int)cudaMemcpyFromSymbol(out, tc::g_gemm_trace, sizeof(unsigned long long) * 1024 * 8);
+}
+#endif
 }  // namespace nova
