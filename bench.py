@@ -1149,7 +1149,9 @@ def gemm_trace(args):
     from nova_winograd import ops
     lib = ops.get_lib()
     try:
-        tr = lib.nova_debug_gemm_trace
+        # NOVA_GEMM_PAIR=1 routes eligible launches to the SM-pair kernel.
+        tr = (lib.nova_debug_gemm2_trace if os.environ.get("NOVA_GEMM_PAIR") == "1"
+              else lib.nova_debug_gemm_trace)
     except AttributeError:
         raise SystemExit("gemm-trace: the library was built without -DNOVA_GEMM_TRACE")
     tr.restype = ctypes.c_int
@@ -1162,6 +1164,8 @@ def gemm_trace(args):
             "epilogue0_wait_accumulator", "epilogue1_wait_accumulator",
             "epilogue0_wait_slab_store_read", "cta_total"]
     nsm = torch.cuda.get_device_properties(device).multi_processor_count
+    if os.environ.get("NOVA_GEMM_PAIR") == "1":
+        nsm -= nsm % 2  # one CTA per SM of the pairs
     out = {"unit": f"us at {args.trace_mhz} MHz (SM-clock cycles / MHz)"}
     for B in (128, 256):
         shapes = [l for l in LAYERS if l[0] in ("conv4_x", "conv5_x")]

@@ -31,6 +31,7 @@
 //   first drains the MMAs it issued and the pair meets at a cluster barrier
 //   before TMEM is released.
 #include <algorithm>
+#include <cstdlib>
 
 #include "nova_internal.h"
 #include "nova_tc_ptx.cuh"
@@ -49,6 +50,15 @@ constexpr int kTmemCols = 512;
 constexpr int kSlabCols = 64;
 constexpr int kSmemLimit = 227 * 1024;
 
+#ifdef NOVA_GEMM_TRACE
+__device__ unsigned long long g_gemm2_trace[1024][8];
+#define TR_T0(v) const long long v = clock64()
+#define TR_ADD(slot, t0) atomicAdd(&g_gemm2_trace[blockIdx.x & 1023][slot], (unsigned long long)(clock64() - (t0)))
+#else
+#define TR_T0(v)
+#define TR_ADD(slot, t0)
+#endif
+
 struct Params {
   long long BP;
   int C, K, BN;
@@ -57,6 +67,7 @@ struct Params {
   int n_cblk;
   long long total_tiles;
   int stages;
+  int epi_split;  // 1: both epilogue warpgroups drain every tile, one half of its columns each
   int* status;
 };
 
@@ -152,7 +163,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(smem_u32(&tfull[a]), 1);
-      mbar_init(smem_u32(&tempty[a]), 8);  // 4 epilogue warps x 2 CTAs
+      // 4 epilogue warps x 2 CTAs, or 8 x 2 when both warpgroups drain every tile
+      mbar_init(smem_u32(&tempty[a]), p.epi_split ? 16 : 8);
     }
     mbar_init(smem_u32(drain), 1);
     *abort_flag = 0;
@@ -174,6 +186,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   const long long tiles_per_pos = (long long)p.n_bp_tiles * p.n_k_tiles;
   const long long t0 = cluster_id_x(), dt = n_clusters_x();
   pdl_wait();
+  TR_T0(tk0);
 
   if (warp == 0) {
     if (lane == 0) {
@@ -190,10 +203,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         const int bp_row = bpt * 2 * kBM + (int)rank * kBM;
         const int k_row = kt * p.BN + (int)rank * half_n;
         for (int cb = 0; cb < p.n_cblk; ++cb) {
+          TR_T0(tw0);
           if (!mbar_wait(smem_u32(&empty[s]), ph ^ 1u, abort_flag, p.status, kDevTimeoutProducer)) {
             ok = false;
             break;
           }
+          TR_ADD(0, tw0);
           const uint32_t sa = smem_u32(base + (size_t)s * stage_bytes);
           const uint32_t fb = map_to_rank(smem_u32(&full[s]), 0);
           if (leader) mbar_expect_tx(smem_u32(&full[s]), 2u * stage_bytes);
@@ -232,15 +247,19 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       for (long long t = t0; t < p.total_tiles && ok; t += dt, ++it) {
         const uint32_t acc = it & 1u;
         const uint32_t aph = (it >> 1) & 1u;
+        TR_T0(tw1);
         if (!mbar_wait(smem_u32(&tempty[acc]), aph ^ 1u, abort_flag, p.status, kDevTimeoutMma))
           break;
+        TR_ADD(1, tw1);
         tc_fence_after();
         const uint32_t dcol = tmem_base + acc * (uint32_t)p.BN;
         for (int cb = 0; cb < p.n_cblk; ++cb) {
+          TR_T0(tw2);
           if (!mbar_wait(smem_u32(&full[s]), ph, abort_flag, p.status, kDevTimeoutMma)) {
             ok = false;
             break;
           }
+          TR_ADD(2, tw2);
           tc_fence_after();
           const uint32_t sa = smem_u32(base + (size_t)s * stage_bytes);
           const uint64_t ad = smem_desc_sw128(sa);
@@ -265,23 +284,31 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     const int eg = (warp - 2) >> 2;
     const uint32_t tempty_leader[2] = {map_to_rank(smem_u32(&tempty[0]), 0),
                                        map_to_rank(smem_u32(&tempty[1]), 0)};
-    uint32_t it = eg;
-    for (long long t = t0 + (long long)eg * dt; t < p.total_tiles; t += 2ll * dt, it += 2) {
+    const int tstep = p.epi_split ? 1 : 2;
+    const int jlo = p.epi_split ? eg * (p.BN >> 1) : 0;
+    const int jhi = p.epi_split ? jlo + (p.BN >> 1) : p.BN;
+    uint32_t it = p.epi_split ? 0u : (uint32_t)eg;
+    for (long long t = t0 + (p.epi_split ? 0ll : (long long)eg * dt); t < p.total_tiles;
+         t += (long long)tstep * dt, it += tstep) {
       const int pos = (int)(t / tiles_per_pos);
       const long long rem = t % tiles_per_pos;
       const int bpt = (int)(rem / p.n_k_tiles);
       const int kt = (int)(rem % p.n_k_tiles);
       const uint32_t acc = it & 1u;
       const uint32_t aph = (it >> 1) & 1u;
+      TR_T0(tw3);
       if (!mbar_wait(smem_u32(&tfull[acc]), aph, abort_flag, p.status, kDevTimeoutEpilogue)) break;
+      if (q == 0 && lane == 0) TR_ADD(3 + eg, tw3);
       tc_fence_after();
       const uint32_t taddr = tmem_base + ((uint32_t)(q * 32) << 16) + acc * (uint32_t)p.BN;
       uint8_t* slab = out_stage + (eg * 4 + q) * slab_bytes;
       uint8_t* my_row = slab + lane * 128;
       const int row0 = bpt * 2 * kBM + (int)rank * kBM + q * 32;
-      for (int h0 = 0; h0 < p.BN; h0 += kSlabCols) {
+      for (int h0 = jlo; h0 < jhi; h0 += kSlabCols) {
+        TR_T0(tw5);
         if (lane == 0) bulk_wait_read_all();
         __syncwarp();
+        if (q == 0 && lane == 0 && eg == 0) TR_ADD(5, tw5);
         for (int j = h0; j < h0 + kSlabCols; j += 32) {
           uint32_t r[32];
           tmem_ld32(taddr + j, r);
@@ -296,7 +323,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             *reinterpret_cast<uint4*>(my_row + (((c_base + v) ^ (lane & 7)) << 4)) = w;
           }
         }
-        if (h0 + kSlabCols >= p.BN) {
+        if (h0 + kSlabCols >= jhi) {
           // This warp's TMEM quarter of the accumulator has been read.
           tc_fence_before();
           __syncwarp();
@@ -315,6 +342,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
 
   tc_fence_before();
   __syncthreads();
+  if (threadIdx.x == 0) TR_ADD(6, tk0);
   cluster_sync();  // the leader's MMAs (reading both CTAs) have drained
   pdl_trigger();
   if (warp == 1) {
@@ -326,6 +354,16 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
 }
 
 }  // namespace tc2
+
+#ifdef NOVA_GEMM_TRACE
+extern "C" __attribute__((visibility("default"))) int nova_debug_gemm2_trace(unsigned long long* out, int reset) {
+  if (reset) {
+    static unsigned long long z[1024][8];
+    return (int)cudaMemcpyToSymbol(tc2::g_gemm2_trace, z, sizeof(z));
+  }
+  return (int)cudaMemcpyFromSymbol(out, tc2::g_gemm2_trace, sizeof(unsigned long long) * 1024 * 8);
+}
+#endif
 
 bool tc2_gemm_eligible(const TcGemmPlan& plan, long long BP) {
   // TMA-store epilogue needs BN % 64 == 0; U halves of BN/2 rows.
@@ -349,6 +387,13 @@ cudaError_t tc2_gemm_run(const TcGemmPlan& plan, const __half* V, __half* M, lon
   p.n_k_tiles = plan.K / plan.BN;
   p.n_cblk = (plan.C + tc2::kBK - 1) / tc2::kBK;
   p.total_tiles = 64ll * p.n_bp_tiles * p.n_k_tiles;
+  {
+    // The 1-SM kernel's rule: short reductions only; NOVA_GEMM_EPI_SPLIT=0
+    // turns it off, =2 forces it wherever the shape allows.
+    const char* e = std::getenv("NOVA_GEMM_EPI_SPLIT");
+    const int env = e ? std::atoi(e) : 1;
+    p.epi_split = env && (plan.BN / 2) % 64 == 0 && (env == 2 || p.n_cblk <= 4);
+  }
   p.status = dev_status;
   const int stage_bytes = tc2::kBM * tc2::kBK * 2 + (plan.BN / 2) * tc2::kBK * 2;
   const int out_bytes = 8 * 32 * std::min(plan.BN, tc2::kSlabCols) * 2;
