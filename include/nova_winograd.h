@@ -120,6 +120,25 @@ int nova_output_transform_v2(const void* d_M_gemm, void* d_output, int batch, in
 int nova_batched_gemm_v2(nova_handle_t h, const void* d_V_gemm, void* d_M_gemm, int BP,
                          void* stream);
 
+/* Channels-last (NHWC) forward.  No reference counterpart: the reference takes
+ * NCHW activations only (csrc/nova_winograd.hip:141-205, 264-328).
+ * d_input is [batch][H][W][C] (16-byte aligned, C % 8 == 0) and d_output
+ * [batch][H_out][W_out][K] (4-byte aligned, K even), FP16; V and M have the NCHW path's layout and size
+ * (nova_workspace_bytes), and the GEMM is the same, so outputs equal the NCHW
+ * path's (up to the sign of an exact zero).  Never takes the fused path.
+ * Returns NOVA_ERR_INVALID_ARGUMENT for other C, K or alignments. */
+int nova_forward_nhwc_v2(nova_handle_t h, const void* d_input, void* d_output, int batch, int H,
+                         int W, int pad, void* stream);
+int nova_forward_workspace_nhwc_v2(nova_handle_t h, const void* d_input, void* d_output,
+                                   void* d_V_gemm, void* d_M_gemm, int batch, int H, int W,
+                                   int pad, int nh, int nw, void* stream);
+/* Stage entries of the NHWC path (the layouts of V and M as nova_input_transform_v2 /
+ * nova_output_transform_v2). */
+int nova_input_transform_nhwc_v2(const void* d_input, void* d_V_gemm, int batch, int C, int H,
+                                 int W, int pad, int nh, int nw, int BP, void* stream);
+int nova_output_transform_nhwc_v2(const void* d_M_gemm, void* d_output, int batch, int K,
+                                  int H_out, int W_out, int nh, int nw, int BP, void* stream);
+
 /* Bytes of caller workspace nova_forward_workspace needs (V + M), the
  * reference's sizing (csrc/nova_winograd_fused.hip:524-534 for the 3-pass case). */
 long long nova_workspace_bytes(nova_handle_t h, int batch, int H, int W, int pad);

@@ -295,6 +295,42 @@ int run_forward(Context* ctx, const void* x, void* y, void* V, void* M, int B, i
   return ok(ctx);
 }
 
+// The three passes on channels-last activations: x [B][H][W][C] and
+// y [B][H_out][W_out][K], C and K even; never the fused kernel.
+int run_forward_nhwc(Context* ctx, const void* x, void* y, void* V, void* M, int B, int H, int W,
+                     int pad, cudaStream_t s) {
+  if (B == 0) return ok(ctx);
+  if (ctx->C % 8 || ctx->K % 2)
+    return fail(ctx, NOVA_ERR_INVALID_ARGUMENT,
+                "forward_nhwc: C must be a multiple of 8 and K even");
+  if (reinterpret_cast<uintptr_t>(x) % 16 || reinterpret_cast<uintptr_t>(y) % 4)
+    return fail(ctx, NOVA_ERR_INVALID_ARGUMENT,
+                "forward_nhwc: x must be 16-byte and y 4-byte aligned");
+  int nh, nw, H_out, W_out;
+  live_tiling(H, W, pad, &nh, &nw, &H_out, &W_out);
+  const long long BP = (long long)B * nh * nw;
+  __half* Vh = static_cast<__half*>(V);
+  __half* Mh = static_cast<__half*>(M);
+  cudaError_t e = launch_input_transform_nhwc(static_cast<const __half*>(x), Vh, B, ctx->C, H, W,
+                                              pad, nh, nw, BP, s);
+  if (e != cudaSuccess) return cuda_fail(ctx, e, "forward_nhwc: input transform");
+  const int path = choose_path(ctx);
+  if (path == 1) {
+    const char* why = "";
+    e = tc_gemm_run(ctx->plan, Vh, Mh, BP, ctx->d_status, ctx->num_sms, s, &why);
+    if (e != cudaSuccess)
+      return fail(ctx, NOVA_ERR_CUDA, std::string("forward_nhwc: tcgen05 GEMM: ") + why);
+  } else {
+    e = launch_gemm_simt(Vh, ctx->U, Mh, BP, ctx->C, ctx->K, s);
+    if (e != cudaSuccess) return cuda_fail(ctx, e, "forward_nhwc: SIMT GEMM");
+  }
+  e = launch_output_transform_nhwc(Mh, static_cast<__half*>(y), B, ctx->K, H_out, W_out, nh, nw,
+                                   BP, s);
+  if (e != cudaSuccess) return cuda_fail(ctx, e, "forward_nhwc: output transform");
+  ctx->last_path = path;
+  return ok(ctx);
+}
+
 size_t live_workspace_bytes(const Context* ctx, int B, int H, int W, int pad) {
   int nh, nw, H_out, W_out;
   live_tiling(H, W, pad, &nh, &nw, &H_out, &W_out);
@@ -305,7 +341,7 @@ size_t live_workspace_bytes(const Context* ctx, int B, int H, int W, int pad) {
 }
 
 int forward_internal_ws(Context* ctx, const void* x, void* y, int B, int H, int W, int pad,
-                        cudaStream_t s) {
+                        cudaStream_t s, bool nhwc = false) {
   int rc = check_forward_args(ctx, x, y, B, H, W, pad);
   if (rc) return rc;
   DeviceGuard g(ctx->device);
@@ -322,11 +358,13 @@ int forward_internal_ws(Context* ctx, const void* x, void* y, int B, int H, int 
   live_tiling(H, W, pad, &nh, &nw, &H_out, &W_out);
   const size_t BP = (size_t)B * nh * nw;
   const size_t voff = (64 * (size_t)ctx->C * BP * 2 + 255) & ~size_t(255);
-  return run_forward(ctx, x, y, ctx->ws, static_cast<char*>(ctx->ws) + voff, B, H, W, pad, s);
+  void* Mp = static_cast<char*>(ctx->ws) + voff;
+  return nhwc ? run_forward_nhwc(ctx, x, y, ctx->ws, Mp, B, H, W, pad, s)
+              : run_forward(ctx, x, y, ctx->ws, Mp, B, H, W, pad, s);
 }
 
 int forward_caller_ws(Context* ctx, const void* x, void* y, void* V, void* M, int B, int H, int W,
-                      int pad, int nh, int nw, cudaStream_t s) {
+                      int pad, int nh, int nw, cudaStream_t s, bool nhwc = false) {
   int rc = check_forward_args(ctx, x, y, B, H, W, pad);
   if (rc) return rc;
   if (B > 0 && (!V || !M)) return fail(ctx, NOVA_ERR_INVALID_ARGUMENT, "forward: null workspace");
@@ -336,7 +374,8 @@ int forward_caller_ws(Context* ctx, const void* x, void* y, void* V, void* M, in
     return fail(ctx, NOVA_ERR_WORKSPACE,
                 "forward_workspace: nh*nw smaller than the tiles the output needs");
   DeviceGuard g(ctx->device);
-  return run_forward(ctx, x, y, V, M, B, H, W, pad, s);
+  return nhwc ? run_forward_nhwc(ctx, x, y, V, M, B, H, W, pad, s)
+              : run_forward(ctx, x, y, V, M, B, H, W, pad, s);
 }
 
 }  // namespace
@@ -506,6 +545,48 @@ NOVA_EXPORT int nova_forward_workspace_v2(nova_handle_t h, const void* d_input, 
                                           int pad, int nh, int nw, void* stream) {
   return nova::forward_caller_ws(as_ctx(h), d_input, d_output, d_V_gemm, d_M_gemm, batch, H, W,
                                  pad, nh, nw, as_stream(stream));
+}
+
+NOVA_EXPORT int nova_forward_nhwc_v2(nova_handle_t h, const void* d_input, void* d_output,
+                                     int batch, int H, int W, int pad, void* stream) {
+  return nova::forward_internal_ws(as_ctx(h), d_input, d_output, batch, H, W, pad,
+                                   as_stream(stream), true);
+}
+
+NOVA_EXPORT int nova_forward_workspace_nhwc_v2(nova_handle_t h, const void* d_input,
+                                               void* d_output, void* d_V_gemm, void* d_M_gemm,
+                                               int batch, int H, int W, int pad, int nh, int nw,
+                                               void* stream) {
+  return nova::forward_caller_ws(as_ctx(h), d_input, d_output, d_V_gemm, d_M_gemm, batch, H, W,
+                                 pad, nh, nw, as_stream(stream), true);
+}
+
+NOVA_EXPORT int nova_input_transform_nhwc_v2(const void* d_input, void* d_V_gemm, int batch, int C,
+                                             int H, int W, int pad, int nh, int nw, int BP,
+                                             void* stream) {
+  if (!d_input || !d_V_gemm || batch <= 0 || C <= 0 || C % 8 || H <= 0 || W <= 0 || pad < 0 ||
+      nh <= 0 || nw <= 0 || (long long)BP < (long long)batch * nh * nw ||
+      reinterpret_cast<uintptr_t>(d_input) % 16)
+    return nova::fail(nullptr, NOVA_ERR_INVALID_ARGUMENT, "input_transform_nhwc: bad arguments");
+  cudaError_t e = nova::launch_input_transform_nhwc(static_cast<const __half*>(d_input),
+                                                    static_cast<__half*>(d_V_gemm), batch, C, H, W,
+                                                    pad, nh, nw, BP, as_stream(stream));
+  if (e != cudaSuccess) return nova::cuda_fail(nullptr, e, "input_transform_nhwc");
+  return nova::ok(nullptr);
+}
+
+NOVA_EXPORT int nova_output_transform_nhwc_v2(const void* d_M_gemm, void* d_output, int batch,
+                                              int K, int H_out, int W_out, int nh, int nw, int BP,
+                                              void* stream) {
+  if (!d_M_gemm || !d_output || batch <= 0 || K <= 0 || K % 2 || H_out <= 0 || W_out <= 0 ||
+      nh <= 0 || nw <= 0 || (long long)BP < (long long)batch * nh * nw ||
+      reinterpret_cast<uintptr_t>(d_output) % 4)
+    return nova::fail(nullptr, NOVA_ERR_INVALID_ARGUMENT, "output_transform_nhwc: bad arguments");
+  cudaError_t e = nova::launch_output_transform_nhwc(static_cast<const __half*>(d_M_gemm),
+                                                     static_cast<__half*>(d_output), batch, K,
+                                                     H_out, W_out, nh, nw, BP, as_stream(stream));
+  if (e != cudaSuccess) return nova::cuda_fail(nullptr, e, "output_transform_nhwc");
+  return nova::ok(nullptr);
 }
 
 NOVA_EXPORT int nova_batched_gemm_v2(nova_handle_t h, const void* d_V_gemm, void* d_M_gemm,

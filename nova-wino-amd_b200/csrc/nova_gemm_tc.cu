@@ -419,6 +419,8 @@ static int pick_bn(int K) {
 
 }  // namespace tc
 
+TensorMapEncodeFn tensor_map_encode_fn() { return tc::get_encode_fn(); }
+
 bool tc_encode_operand_map(CUtensorMap* map, const void* ptr, int C, long long rows,
                            int box_rows) {
   return tc::encode_operand_map(map, ptr, C, rows, box_rows);

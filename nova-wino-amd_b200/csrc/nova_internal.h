@@ -101,6 +101,22 @@ cudaError_t launch_output_transform_fast(const __half* M, __half* y, int K, int 
                                          long long BP, cudaStream_t s);
 cudaError_t launch_gemm_simt(const __half* V, const __half* U, __half* M, long long BP, int C,
                              int K, cudaStream_t s);
+// cuTensorMapEncodeTiled through the runtime's driver entry point (null if
+// the driver does not provide it); defined in nova_gemm_tc.cu.
+using TensorMapEncodeFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                       const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                       const cuuint32_t*, CUtensorMapInterleave,
+                                       CUtensorMapSwizzle, CUtensorMapL2promotion,
+                                       CUtensorMapFloatOOBfill);
+TensorMapEncodeFn tensor_map_encode_fn();
+
+// Channels-last (NHWC) activations, whole batch (nova_nhwc.cu): the same V / M
+// layouts as the NCHW kernels.  Input transform: C % 8 == 0 and x 16-byte
+// aligned (TMA box loads); output transform: K even, y 4-byte aligned.
+cudaError_t launch_input_transform_nhwc(const __half* x, __half* V, int B, int C, int H, int W,
+                                        int pad, int nh, int nw, long long BP, cudaStream_t s);
+cudaError_t launch_output_transform_nhwc(const __half* M, __half* y, int B, int K, int H_out,
+                                         int W_out, int nh, int nw, long long BP, cudaStream_t s);
 
 // Tensor-core (tcgen05 + TMA) batched GEMM.
 struct TcGemmPlan {

@@ -23,8 +23,8 @@ import torch
 import torch.nn as nn
 import torch.nn.functional as F
 
-from nova_winograd.ops import (check, compute_tiling, create_handle, get_lib, ptr, stream_ptr,
-                               _ensure_lib)
+from nova_winograd.ops import (check, compute_tiling, create_handle, get_lib, nhwc_eligible, ptr,
+                               stream_ptr, _ensure_lib)
 
 
 def _weight_grad(inp, weight, grad_out, padding):
@@ -103,7 +103,9 @@ class NovaWinogradFunction(torch.autograd.Function):
         ctx.save_for_backward(input, weight, bias)
         ctx.padding = padding
         ctx.weight_grad = getattr(handle_holder, "weight_grad", "fp32")
-        x = input.half().contiguous() if input.dtype != torch.float16 else input.contiguous()
+        x = input.half() if input.dtype != torch.float16 else input
+        if not (x.is_contiguous() or nhwc_eligible(x, weight.shape[0])):
+            x = x.contiguous()
         return handle_holder._native_forward(x, bias)
 
     @staticmethod
@@ -140,8 +142,11 @@ def _raw_stream(device_index):
 class NovaWinogradConv2d(nn.Module):
     """Drop-in replacement for nn.Conv2d (3x3, stride 1) using NOVA F(6,3).
 
-    Input must be float16 and contiguous.  Weights are stored in float32 and
-    transformed on first use and again whenever ``weight._version`` changes.
+    Input must be float16 and contiguous, or channels-last: channels-last input
+    gives channels-last output, through the NHWC kernels when C % 8 == 0 and the
+    output channels are even (else through an on-device copy to NCHW).  Weights
+    are stored in float32 and transformed on first use and again whenever
+    ``weight._version`` changes.
     """
 
     def __init__(self, in_channels, out_channels, kernel_size=3, padding=1, bias=False):
@@ -205,13 +210,21 @@ class NovaWinogradConv2d(nn.Module):
         return nh, nw, H_out, W_out
 
     def _native_forward(self, x, bias):
-        # Steady state: same input geometry and device, same weight tensor and
-        # version as the call that filled _fast -- skip straight to the launch.
+        # x is contiguous (NCHW) or channels-last; channels-last input the NHWC
+        # kernels cannot take goes through NCHW and comes back channels-last.
+        nhwc = not x.is_contiguous()
+        if nhwc and not nhwc_eligible(x, self.out_channels):
+            out = self._native_forward(x.contiguous(), bias)
+            return out.contiguous(memory_format=torch.channels_last)
+        # Steady state: same input geometry, layout and device, same weight
+        # tensor and version as the call that filled _fast -- skip straight to
+        # the launch.
         fast = self._fast
         if (fast is not None and fast[0] == x.shape and fast[1] == x.device
                 and fast[2] == self.weight._version and fast[3] == self.weight.data_ptr()
-                and fast[4] == torch.cuda.current_device()):
-            output = torch.empty(fast[5], dtype=torch.float16, device=x.device)
+                and fast[4] == torch.cuda.current_device() and fast[10] == nhwc):
+            output = torch.empty(fast[5], dtype=torch.float16, device=x.device,
+                                 memory_format=fast[11])
             status = fast[6](self._handle, x.data_ptr(), output.data_ptr(), fast[7], fast[8],
                              *fast[9], _raw_stream(fast[4]))
             if status:
@@ -229,21 +242,23 @@ class NovaWinogradConv2d(nn.Module):
         if dev != self.weight.device:
             raise ValueError("input and weight are on different devices")
         if dev.index == torch.cuda.current_device():
-            output = self._launch(x, B, H, W)
+            output = self._launch(x, B, H, W, nhwc)
         else:
             with torch.cuda.device(dev):
-                output = self._launch(x, B, H, W)
+                output = self._launch(x, B, H, W, nhwc)
         if bias is not None:
             output = output + bias.half().view(1, -1, 1, 1)
         return output
 
-    def _launch(self, x, B, H, W):
+    def _launch(self, x, B, H, W, nhwc=False):
         """Forward on the current device and stream (the input's device)."""
         self._ensure_handle()
         nh, nw, H_out, W_out = self._ensure_workspace(B, H, W)
+        fmt = torch.channels_last if nhwc else torch.contiguous_format
         output = torch.empty(B, self.out_channels, H_out, W_out, dtype=torch.float16,
-                             device=x.device)
-        fn = get_lib().nova_forward_workspace_v2
+                             device=x.device, memory_format=fmt)
+        lib = get_lib()
+        fn = lib.nova_forward_workspace_nhwc_v2 if nhwc else lib.nova_forward_workspace_v2
         ints = (B, H, W, self.padding, nh, nw)
         status = fn(self._handle, x.data_ptr(), output.data_ptr(), self._V_gemm.data_ptr(),
                     self._M_gemm.data_ptr(), *ints, _raw_stream(x.device.index))
@@ -251,14 +266,14 @@ class NovaWinogradConv2d(nn.Module):
             check(status, "nova_forward_workspace")
         self._fast = (x.shape, x.device, self.weight._version, self.weight.data_ptr(),
                       x.device.index, tuple(output.shape), fn, self._V_gemm.data_ptr(),
-                      self._M_gemm.data_ptr(), ints)
+                      self._M_gemm.data_ptr(), ints, nhwc, fmt)
         return output
 
     def forward(self, x):
         if x.dtype != torch.float16:
             raise TypeError(f"Input must be float16, got {x.dtype}")
-        if not x.is_contiguous():
-            raise ValueError("Input must be contiguous")
+        if not (x.is_contiguous() or x.is_contiguous(memory_format=torch.channels_last)):
+            raise ValueError("Input must be contiguous (or channels-last)")
         return self._native_forward(x, self.bias)
 
     def __del__(self):
@@ -302,7 +317,7 @@ class NovaWinogradConv2dTrainable(NovaWinogradConv2d):
     weight_grad = "fp32"
 
     def forward(self, x):
-        if not x.is_contiguous():
+        if not (x.is_contiguous() or x.is_contiguous(memory_format=torch.channels_last)):
             x = x.contiguous()
         if x.dtype != torch.float16:
             x = x.half()

@@ -55,6 +55,10 @@ SIGNATURES = {
     "nova_input_transform_v2": (c_int, [c_void_p, c_void_p] + [c_int] * 8 + [c_void_p]),
     "nova_output_transform_v2": (c_int, [c_void_p, c_void_p] + [c_int] * 7 + [c_void_p]),
     "nova_batched_gemm_v2": (c_int, [c_void_p, c_void_p, c_void_p, c_int, c_void_p]),
+    "nova_forward_nhwc_v2": (c_int, [c_void_p, c_void_p, c_void_p] + [c_int] * 4 + [c_void_p]),
+    "nova_forward_workspace_nhwc_v2": (c_int, [c_void_p] * 5 + [c_int] * 6 + [c_void_p]),
+    "nova_input_transform_nhwc_v2": (c_int, [c_void_p, c_void_p] + [c_int] * 8 + [c_void_p]),
+    "nova_output_transform_nhwc_v2": (c_int, [c_void_p, c_void_p] + [c_int] * 7 + [c_void_p]),
     "nova_workspace_bytes": (c_longlong, [c_void_p, c_int, c_int, c_int, c_int]),
     "nova_set_path": (c_int, [c_void_p, c_int]),
     "nova_get_path": (c_int, [c_void_p]),
@@ -170,11 +174,21 @@ def create_handle(device=None):
     return h
 
 
+def nhwc_eligible(x, K):
+    """True when x is a channels-last [B, C, H, W] tensor (and not also plain
+    contiguous) that the NHWC kernels take: C % 8 == 0, K even, a 16-byte
+    aligned base."""
+    return (x.dim() == 4 and not x.is_contiguous()
+            and x.is_contiguous(memory_format=torch.channels_last)
+            and x.shape[1] % 8 == 0 and K % 2 == 0 and x.data_ptr() % 16 == 0)
+
+
 def nova_forward(input_fp16, weight_fp32, padding=1):
     """Functional API: NOVA Winograd F(6,3) forward (reference ops.py:147-176).
 
     Args:
-        input_fp16:  [B, C, H, W] float16 CUDA tensor, contiguous.
+        input_fp16:  [B, C, H, W] float16 CUDA tensor, contiguous, or channels-last
+                     with C % 8 == 0 and K even (then the output is channels-last).
         weight_fp32: [K, C, 3, 3] float32 CUDA tensor, contiguous.
         padding:     convolution padding (default 1).
 
@@ -191,7 +205,8 @@ def nova_forward(input_fp16, weight_fp32, padding=1):
         raise TypeError("input must be a float16 CUDA tensor")
     if not (weight_fp32.is_cuda and weight_fp32.dtype == torch.float32):
         raise TypeError("weight must be a float32 CUDA tensor")
-    if not (input_fp16.is_contiguous() and weight_fp32.is_contiguous()):
+    nhwc = nhwc_eligible(input_fp16, weight_fp32.shape[0])
+    if not ((input_fp16.is_contiguous() or nhwc) and weight_fp32.is_contiguous()):
         raise ValueError("input and weight must be contiguous")
     if weight_fp32.dim() != 4 or tuple(weight_fp32.shape[2:]) != (3, 3):
         raise ValueError("weight must be [K, C, 3, 3]")
@@ -201,14 +216,16 @@ def nova_forward(input_fp16, weight_fp32, padding=1):
         raise ValueError(f"weight has {weight_fp32.shape[1]} input channels, input has {C}")
     nh, nw, H_out, W_out = compute_tiling(H, W, padding)
     device = input_fp16.device
-    output = torch.empty(B, K, H_out, W_out, dtype=torch.float16, device=device)
+    fmt = torch.channels_last if nhwc else torch.contiguous_format
+    output = torch.empty(B, K, H_out, W_out, dtype=torch.float16, device=device,
+                         memory_format=fmt)
+    fwd = _lib.nova_forward_nhwc_v2 if nhwc else _lib.nova_forward_v2
     with torch.cuda.device(device):
         s = stream_ptr()
         handle = create_handle(device)
         try:
             check(_lib.nova_set_weights_v2(handle, ptr(weight_fp32), K, C, s), "nova_set_weights")
-            check(_lib.nova_forward_v2(handle, ptr(input_fp16), ptr(output), B, H, W, padding, s),
-                  "nova_forward")
+            check(fwd(handle, ptr(input_fp16), ptr(output), B, H, W, padding, s), "nova_forward")
             torch.cuda.current_stream().synchronize()
         finally:
             _lib.nova_destroy(handle)

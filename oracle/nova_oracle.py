@@ -306,6 +306,34 @@ def gemm_scale(U: np.ndarray, V: np.ndarray) -> np.ndarray:
     return np.matmul(np.abs(V.astype(np.float64)), np.abs(U.astype(np.float64)))
 
 
+def input_transform_scale(x: np.ndarray, nh: int, nw: int, pad: int) -> np.ndarray:
+    """Sum of the magnitudes of the 16 terms behind each V[pos][bp][c]
+    (|B|^T |d| |B|), the scale within_fp32_reordering takes for V."""
+    Ba = np.abs(matrices("ref")[1])
+    d = np.abs(input_tiles(x, nh, nw, pad)).astype(np.float64)
+    v = Ba.T @ d @ Ba
+    return v.transpose(4, 5, 0, 2, 3, 1).reshape(64, -1, x.shape[1])
+
+
+def filter_transform_scale(w: np.ndarray) -> np.ndarray:
+    """Sum of the magnitudes of the 9 terms behind each U[pos][c][k]
+    (|G| |w| |G|^T), the scale within_fp32_reordering takes for U."""
+    Ga = np.abs(matrices("ref")[2])
+    u = Ga @ np.abs(w).astype(np.float64) @ Ga.T
+    return u.transpose(2, 3, 1, 0).reshape(64, w.shape[1], w.shape[0])
+
+
+def output_transform_scale(M: np.ndarray, B: int, nh: int, nw: int, Ho: int,
+                           Wo: int) -> np.ndarray:
+    """Sum of the magnitudes of the terms behind each y[b][k][h][w]
+    (|A|^T |M| |A|), the scale within_fp32_reordering takes for y."""
+    Aa = np.abs(matrices("ref")[0])
+    K = M.shape[2]
+    m = np.abs(M.astype(np.float64)).reshape(8, 8, B, nh, nw, K).transpose(2, 5, 3, 4, 0, 1)
+    y = (Aa @ m @ Aa.T).transpose(0, 1, 2, 4, 3, 5).reshape(B, K, nh * 6, nw * 6)
+    return y[:, :, :Ho, :Wo]
+
+
 def within_fp32_reordering(a: np.ndarray, b: np.ndarray, scale: np.ndarray,
                            terms: int) -> np.ndarray:
     """True where FP16 results a and b can both come from the same exact value

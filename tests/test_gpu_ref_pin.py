@@ -73,30 +73,16 @@ def ref_tiling(H, W, pad):
     return tuple(t.value for t in v)
 
 
-def abs_mats():
-    A, Bm, G = o.matrices("ref")
-    return np.abs(A), np.abs(Bm), np.abs(G)
-
-
 def input_scale(x, nh, nw, pad):
-    _, Ba, _ = abs_mats()
-    d = np.abs(o.input_tiles(x, nh, nw, pad)).astype(np.float64)
-    v = Ba.T @ d @ Ba
-    return v.transpose(4, 5, 0, 2, 3, 1).reshape(64, -1, x.shape[1])
+    return o.input_transform_scale(x, nh, nw, pad)
 
 
 def filter_scale(w):
-    _, _, Ga = abs_mats()
-    u = Ga @ np.abs(w).astype(np.float64) @ Ga.T
-    return u.transpose(2, 3, 1, 0).reshape(64, w.shape[1], w.shape[0])
+    return o.filter_transform_scale(w)
 
 
 def output_scale(M, B, nh, nw, Ho, Wo):
-    Aa, _, _ = abs_mats()
-    K = M.shape[2]
-    m = np.abs(M.astype(np.float64)).reshape(8, 8, B, nh, nw, K).transpose(2, 5, 3, 4, 0, 1)
-    y = (Aa @ m @ Aa.T).transpose(0, 1, 2, 4, 3, 5).reshape(B, K, nh * 6, nw * 6)
-    return y[:, :, :Ho, :Wo]
+    return o.output_transform_scale(M, B, nh, nw, Ho, Wo)
 
 
 def assert_exact(got, want, what):
