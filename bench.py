@@ -349,10 +349,13 @@ def stage_profile(layers, batch, flush, reps=20):
     return out
 
 
-def vendor_layer_times(layers, flush, reps=20):
+def vendor_layer_times(layers, flush, reps=20, channels_last=False):
     """Whole-layer device time of our forward and of torch's FP16 conv2d (cuDNN)
     on the same layer, L2 flushed before each launch (context, like the
-    reference's MIOpen comparison in benchmarks/bench_layers.py)."""
+    reference's MIOpen comparison in benchmarks/bench_layers.py).  With
+    channels_last, also both on the channels-last copy of the input (our NHWC
+    kernels; cuDNN's channels-last kernels), with the NHWC outputs of sampled
+    images checked against the oracle."""
     import torch
     import torch.nn.functional as F
     res = {}
@@ -369,6 +372,26 @@ def vendor_layer_times(layers, flush, reps=20):
         res[name] = {"nova_us": round(ours * 1e3, 1), "cudnn_fp16_us": round(cudnn * 1e3, 1),
                      "nova_eff_tflops": round(fl / ours / 1e9, 1),
                      "cudnn_eff_tflops": round(fl / cudnn / 1e9, 1)}
+        if channels_last:
+            xl = x.contiguous(memory_format=torch.channels_last)
+            wl = w16.contiguous(memory_format=torch.channels_last)
+            with torch.no_grad():
+                for _ in range(3):
+                    F.conv2d(xl, wl, padding=1)
+                yl = conv(xl)
+                ours_cl = time_kernel(lambda: conv(xl), reps, flush)
+                cudnn_cl = time_kernel(lambda: F.conv2d(xl, wl, padding=1), reps, flush)
+            torch.cuda.synchronize()
+            par = sample_parity(name, x, conv.weight, yl.contiguous())
+            res[name].update({
+                "nova_nhwc_us": round(ours_cl * 1e3, 1),
+                "cudnn_fp16_channels_last_us": round(cudnn_cl * 1e3, 1),
+                "nova_nhwc_eff_tflops": round(fl / ours_cl / 1e9, 1),
+                "cudnn_channels_last_eff_tflops": round(fl / cudnn_cl / 1e9, 1),
+                "nhwc_output_channels_last": bool(yl.is_contiguous(
+                    memory_format=torch.channels_last)),
+                "nhwc_parity": {k: par[k] for k in ("images", "rel_l2_vs_oracle", "ok")}})
+            del xl, yl
     return res
 
 
@@ -434,41 +457,49 @@ def roofline_from_stages(stages, peaks, batch=128):
 
 def b1_latency(device, reps=200):
     """Per-layer batch-1 latency (us): back-to-back module calls (host overhead
-    included) and the same call replayed from a CUDA graph (device only)."""
+    included) and the same call replayed from a CUDA graph (device only); the
+    same for the channels-last input (the NHWC kernels) under "nhwc"."""
     import torch
-    layers = build_layers(1, device)
     res = {}
-    for name, C, H, conv, x in layers:
-        for _ in range(20):
-            conv(x)
-        torch.cuda.synchronize()
-        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        s.record()
-        for _ in range(reps):
-            conv(x)
-        e.record()
-        torch.cuda.synchronize()
-        us_eager = s.elapsed_time(e) / reps * 1e3
-        g = torch.cuda.CUDAGraph()
-        st = torch.cuda.Stream()
-        with torch.cuda.stream(st):
-            conv(x)
-            st.synchronize()
-            with torch.cuda.graph(g, stream=st):
-                for _ in range(10):
-                    conv(x)
-        torch.cuda.synchronize()
-        g.replay()
-        torch.cuda.synchronize()
-        s.record()
-        for _ in range(reps // 10):
-            g.replay()
-        e.record()
-        torch.cuda.synchronize()
-        us_graph = s.elapsed_time(e) / reps * 1e3
-        res[name] = {"us_eager": round(us_eager, 2), "us_graph": round(us_graph, 2),
-                     "eff_tflops_graph": round(direct_flops(1, C, C, H) / us_graph / 1e6, 2)}
+    for name, C, H, conv, x in build_layers(1, device):
+        res[name] = _b1_one(conv, x, C, H, reps)
+        res[name]["nhwc"] = _b1_one(conv, x.contiguous(memory_format=torch.channels_last), C, H,
+                                    reps)
     return res
+
+
+def _b1_one(conv, x, C, H, reps):
+    """Eager and graph-replayed batch-1 latency of one layer (see b1_latency)."""
+    import torch
+    for _ in range(20):
+        conv(x)
+    torch.cuda.synchronize()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    for _ in range(reps):
+        conv(x)
+    e.record()
+    torch.cuda.synchronize()
+    us_eager = s.elapsed_time(e) / reps * 1e3
+    g = torch.cuda.CUDAGraph()
+    st = torch.cuda.Stream()
+    with torch.cuda.stream(st):
+        conv(x)
+        st.synchronize()
+        with torch.cuda.graph(g, stream=st):
+            for _ in range(10):
+                conv(x)
+    torch.cuda.synchronize()
+    g.replay()
+    torch.cuda.synchronize()
+    s.record()
+    for _ in range(reps // 10):
+        g.replay()
+    e.record()
+    torch.cuda.synchronize()
+    us_graph = s.elapsed_time(e) / reps * 1e3
+    return {"us_eager": round(us_eager, 2), "us_graph": round(us_graph, 2),
+            "eff_tflops_graph": round(direct_flops(1, C, C, H) / us_graph / 1e6, 2)}
 
 
 class _TorchCuda:
@@ -811,7 +842,7 @@ def run_nova(args):
         stages = stage_profile(layers, batch, flush)
         roofline = roofline_from_stages(stages, peaks, batch)
         lat = b1_latency(device)
-        vendor = vendor_layer_times(layers, flush)
+        vendor = vendor_layer_times(layers, flush, channels_last=True)
         if not args.quick:
             grid = config2_grid(device, flush)
             b256 = gemm_stage_b256(device, flush, peaks)
@@ -999,6 +1030,23 @@ def resnet50_measure(batch, steps, warmup, device, dist, world, rank):
         rec["conv_parity_image0"] = {"convs_checked": len(seen),
                                      "worst_rel_l2_vs_oracle": worst["rel_l2_vs_oracle"],
                                      "all_ok": worst["ok"]}
+    # The same two models channels-last (weights and input): the replaced convs
+    # run the NHWC kernels, the rest of the network cuDNN's channels-last
+    # kernels.  All ranks, weak scaling as above.
+    model = model.to(memory_format=torch.channels_last)
+    ref = ref.to(memory_format=torch.channels_last)
+    x = x.contiguous(memory_format=torch.channels_last)
+    ms_cl, out_cl = timed(model)
+    ms_ref_cl, out_ref_cl = timed(ref)
+    rec["channels_last"] = {
+        "img_s": world * batch * steps / (ms_cl / 1e3), "ms_per_step": ms_cl / steps,
+        "cudnn_same_model_img_s": world * batch * steps / (ms_ref_cl / 1e3),
+        "logits_finite": bool(torch.isfinite(out_cl).all().item()),
+        "logits_rel_diff_vs_cudnn": float(((out_cl.float() - out_ref_cl.float()).norm() /
+                                           out_ref_cl.float().norm()).item()),
+        "logits_rel_diff_vs_nchw": float(((out_cl.float() - out.float()).norm() /
+                                          out.float().norm()).item()),
+    }
     del model, ref, x
     torch.cuda.empty_cache()
     return rec
