@@ -935,7 +935,7 @@ def run_unet_layers(args):
         "config": {"workload": f"{args.workload.split('_')[0]}_unet_3x3_shapes", "layers": [l[0] for l in shapes],
                    "batch_per_gpu": args.batch,
                    "l2": "flushed between steps (write then read 2x L2)"},
-        "per_layer_vs_cudnn": vendor_layer_times(layers, flush),
+        "per_layer_vs_cudnn": vendor_layer_times(layers, flush, channels_last=True),
         "library": __import__("nova_winograd").ops.get_lib().nova_version().decode(),
     })
 
@@ -1157,6 +1157,26 @@ def run_unet_model(args):
         e.record()
         torch.cuda.synchronize()
     e2e_ms = max_over_ranks(dist, s.elapsed_time(e))
+    # Both models channels-last (weights and latent): the replaced convs on the
+    # NHWC kernels, the rest on cuDNN's channels-last kernels.
+    model = model.to(memory_format=torch.channels_last)
+    ref = ref.to(memory_format=torch.channels_last)
+    x = x.contiguous(memory_format=torch.channels_last)
+    ms_cl, out_cl = timed(model)
+    ms_ref_cl, out_ref_cl = timed(ref)
+    channels_last = {
+        "latents_s": world * args.batch * args.steps / (ms_cl / 1e3),
+        "ms_per_step": ms_cl / args.steps,
+        "cudnn_same_model_latents_s": world * args.batch * args.steps / (ms_ref_cl / 1e3),
+        "cudnn_same_model_ms_per_step": ms_ref_cl / args.steps,
+        "output_finite": bool(torch.isfinite(out_cl).all().item()),
+        "output_rel_diff_vs_nchw": float(((out_cl.float() - out.float()).norm() /
+                                          out.float().norm()).item()),
+        # The same comparison for the cuDNN model: how far the network itself
+        # carries summation-order differences between the two layouts.
+        "cudnn_output_rel_diff_channels_last_vs_nchw": float(
+            ((out_ref_cl.float() - out_ref.float()).norm() / out_ref.float().norm()).item()),
+    }
     if rank == 0:
         emit({
             "metric": f"{name} UNet FP16 denoising step, latents/s ({n_rep} 3x3 s1 convs on NOVA F(6,3))",
@@ -1175,6 +1195,7 @@ def run_unet_model(args):
             "cudnn_same_model_latents_s": world * args.batch * args.steps / (ms_ref / 1e3),
             "cudnn_same_model_ms_per_step": ms_ref / args.steps,
             "output_finite": finite, "output_rel_diff_vs_cudnn": rel,
+            "channels_last": channels_last,
             "clocks": clocks,
         })
     if dist is not None:
