@@ -1312,6 +1312,19 @@ def profile_stages(args):
         torch.cuda.synchronize()
         print(f"profile-stages {name} batch {args.batch} (fused): ok")
         return
+    if args.nhwc:
+        # The channels-last stage entries on the same layer.
+        xl = x.contiguous(memory_format=torch.channels_last)
+        yl = y.contiguous(memory_format=torch.channels_last)
+        for _ in range(args.steps):
+            ops.check(lib.nova_input_transform_nhwc_v2(ops.ptr(xl), ops.ptr(V), args.batch, C, H,
+                                                       H, 1, nt, nt, BP, s), "input_transform_nhwc")
+            ops.check(lib.nova_batched_gemm_v2(conv._handle, ops.ptr(V), ops.ptr(M), BP, s), "gemm")
+            ops.check(lib.nova_output_transform_nhwc_v2(ops.ptr(M), ops.ptr(yl), args.batch, C, H,
+                                                        H, nt, nt, BP, s), "output_transform_nhwc")
+        torch.cuda.synchronize()
+        print(f"profile-stages {name} batch {args.batch} (nhwc): ok")
+        return
     for _ in range(args.steps):
         ops.check(lib.nova_input_transform_v2(ops.ptr(x), ops.ptr(V), args.batch, C, H, H, 1,
                                               nt, nt, BP, s), "input_transform")
@@ -1361,6 +1374,8 @@ def main():
                          "3x3 conv shapes one layer at a time against cuDNN")
     ap.add_argument("--fused", action="store_true",
                     help="with --profile-stages: run the fused single kernel instead (C, K <= 64)")
+    ap.add_argument("--nhwc", action="store_true",
+                    help="with --profile-stages: the channels-last stage entries")
     ap.add_argument("--gemm-trace", action="store_true",
                     help="wait breakdown of the GEMM's warp roles (library built with "
                          "-DNOVA_GEMM_TRACE)")
