@@ -70,16 +70,20 @@ struct Params {
 
 // Tile t -> (pos, bp tile, k tile) and its range of reduction blocks.  The
 // split index runs fastest, so with one split the order is (pos, bp, k).
-__device__ __forceinline__ void tile_of(const Params& p, long long t, int& pos, int& bpt, int& kt,
-                                        int& cb0, int& cb1) {
-  const int split = (int)(t % p.n_split);
-  t /= p.n_split;
-  const long long per_pos = (long long)p.n_bp_tiles * p.n_k_tiles;
+// 32-bit unsigned arithmetic: the host keeps total_tiles below 2^31 (64-bit
+// division is a long emulated sequence, and every warp role decodes every
+// tile: at conv2_x that was a measurable share of the MMA issuer's time).
+__device__ __forceinline__ void tile_of(const Params& p, long long t64, int& pos, int& bpt,
+                                        int& kt, int& cb0, int& cb1) {
+  uint32_t t = (uint32_t)t64;
+  const uint32_t split = t % (uint32_t)p.n_split;
+  t /= (uint32_t)p.n_split;
+  const uint32_t per_pos = (uint32_t)p.n_bp_tiles * (uint32_t)p.n_k_tiles;
   pos = (int)(t / per_pos);
-  const long long rem = t % per_pos;
-  bpt = (int)(rem / p.n_k_tiles);
-  kt = (int)(rem % p.n_k_tiles);
-  cb0 = split * p.kb_per_split;
+  const uint32_t rem = t - (uint32_t)pos * per_pos;
+  bpt = (int)(rem / (uint32_t)p.n_k_tiles);
+  kt = (int)(rem - (uint32_t)bpt * (uint32_t)p.n_k_tiles);
+  cb0 = (int)split * p.kb_per_split;
   cb1 = min(p.n_cblk, cb0 + p.kb_per_split);
 }
 
@@ -213,8 +217,8 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
         TR_ADD(1, tw1);
         tc_fence_after();
         const uint32_t dcol = tmem_base + acc * (uint32_t)p.BN;
-        int pos_, bpt_, kt_, cb0, cb1;
-        tile_of(p, t, pos_, bpt_, kt_, cb0, cb1);
+        int pos_, bpt_, kt_, cb0 = 0, cb1 = p.n_cblk;
+        if (p.n_split > 1) tile_of(p, t, pos_, bpt_, kt_, cb0, cb1);
         for (int cb = cb0; cb < cb1; ++cb) {
           TR_T0(tw2);
           if (!mbar_wait(smem_u32(&full[s]), ph, abort_flag, p.status, kDevTimeoutMma)) {
@@ -532,6 +536,10 @@ cudaError_t tc_gemm_run(const TcGemmPlan& plan, const __half* V, __half* M, long
   p.n_split = 1;
   p.kb_per_split = p.n_cblk;
   p.total_tiles = 64ll * p.n_bp_tiles * p.n_k_tiles;
+  if (p.total_tiles >= (1ll << 31)) {
+    *why = "tensor-core GEMM: too many tiles for one launch";
+    return cudaErrorInvalidValue;
+  }
   p.epi_split = epi_split_ok(BN, p.tma_store, (plan.C + tc::kBK - 1) / tc::kBK);
   p.status = dev_status;
   const int stage_bytes = tc::kBM * tc::kBK * 2 + BN * tc::kBK * 2;
@@ -631,6 +639,10 @@ cudaError_t tc_gemm_wgrad_run(const __half* A, const __half* Bop, float* Ug, int
   p.n_split = tc_gemm_wgrad_splits(K, C, BP, num_sms);
   p.kb_per_split = (p.n_cblk + p.n_split - 1) / p.n_split;
   p.total_tiles = base * p.n_split;
+  if (p.total_tiles >= (1ll << 31)) {
+    *why = "weight-gradient GEMM: too many tiles for one launch";
+    return cudaErrorInvalidValue;
+  }
   p.tma_store = 0;
   p.epi_split = epi_split_ok(BN, 0, p.n_cblk);
   p.status = dev_status;

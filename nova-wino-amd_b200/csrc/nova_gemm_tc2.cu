@@ -183,7 +183,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   cluster_sync();  // barriers of both CTAs initialised, TMEM allocated
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
-  const long long tiles_per_pos = (long long)p.n_bp_tiles * p.n_k_tiles;
+  // 32-bit tile arithmetic (the host keeps total_tiles below 2^31).
+  const uint32_t tiles_per_pos = (uint32_t)p.n_bp_tiles * (uint32_t)p.n_k_tiles;
   const long long t0 = cluster_id_x(), dt = n_clusters_x();
   pdl_wait();
   TR_T0(tk0);
@@ -196,10 +197,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       bool ok = true;
       long long issued = 0;
       for (long long t = t0; t < p.total_tiles && ok; t += dt) {
-        const int pos = (int)(t / tiles_per_pos);
-        const long long rem = t % tiles_per_pos;
-        const int bpt = (int)(rem / p.n_k_tiles);
-        const int kt = (int)(rem % p.n_k_tiles);
+        const uint32_t tu = (uint32_t)t;
+        const int pos = (int)(tu / tiles_per_pos);
+        const uint32_t rem = tu - (uint32_t)pos * tiles_per_pos;
+        const int bpt = (int)(rem / (uint32_t)p.n_k_tiles);
+        const int kt = (int)(rem - (uint32_t)bpt * (uint32_t)p.n_k_tiles);
         const int bp_row = bpt * 2 * kBM + (int)rank * kBM;
         const int k_row = kt * p.BN + (int)rank * half_n;
         for (int cb = 0; cb < p.n_cblk; ++cb) {
@@ -290,10 +292,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     uint32_t it = p.epi_split ? 0u : (uint32_t)eg;
     for (long long t = t0 + (p.epi_split ? 0ll : (long long)eg * dt); t < p.total_tiles;
          t += (long long)tstep * dt, it += tstep) {
-      const int pos = (int)(t / tiles_per_pos);
-      const long long rem = t % tiles_per_pos;
-      const int bpt = (int)(rem / p.n_k_tiles);
-      const int kt = (int)(rem % p.n_k_tiles);
+      const uint32_t tu = (uint32_t)t;
+      const int pos = (int)(tu / tiles_per_pos);
+      const uint32_t rem = tu - (uint32_t)pos * tiles_per_pos;
+      const int bpt = (int)(rem / (uint32_t)p.n_k_tiles);
+      const int kt = (int)(rem - (uint32_t)bpt * (uint32_t)p.n_k_tiles);
       const uint32_t acc = it & 1u;
       const uint32_t aph = (it >> 1) & 1u;
       TR_T0(tw3);
@@ -387,6 +390,10 @@ cudaError_t tc2_gemm_run(const TcGemmPlan& plan, const __half* V, __half* M, lon
   p.n_k_tiles = plan.K / plan.BN;
   p.n_cblk = (plan.C + tc2::kBK - 1) / tc2::kBK;
   p.total_tiles = 64ll * p.n_bp_tiles * p.n_k_tiles;
+  if (p.total_tiles >= (1ll << 31)) {
+    *why = "SM-pair GEMM: too many tiles for one launch";
+    return cudaErrorInvalidValue;
+  }
   {
     // The 1-SM kernel's rule: short reductions only; NOVA_GEMM_EPI_SPLIT=0
     // turns it off, =2 forces it wherever the shape allows.

@@ -152,12 +152,12 @@ __global__ void __launch_bounds__(32 * ItGeo<TR, TC>::kWarps, NOVA_NHWC_IT_WARPS
   __shared__ __align__(8) uint64_t bar;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int n_twc = (a.nw + TC - 1) / TC, n_thr = (a.nh + TR - 1) / TR;
-  const long long seg = blockIdx.x;
+  const uint32_t seg = blockIdx.x;  // 32-bit decode (64-bit division is emulated)
   const int cg = blockIdx.y;
-  const int twc = (int)(seg % n_twc);
-  const long long band = seg / n_twc;  // b * n_thr + thr
-  const int thr = (int)(band % n_thr);
-  const long long b = band / n_thr;
+  const int twc = (int)(seg % (uint32_t)n_twc);
+  const uint32_t band = seg / (uint32_t)n_twc;  // b * n_thr + thr
+  const int thr = (int)(band % (uint32_t)n_thr);
+  const long long b = band / (uint32_t)n_thr;
   const int h0 = thr * TR * 6 - a.pad, w0 = twc * TC * 6 - a.pad;
   const uint32_t bar_s = static_cast<uint32_t>(__cvta_generic_to_shared(&bar));
   if (threadIdx.x == 0) {
@@ -285,12 +285,12 @@ __global__ void __launch_bounds__(32 * OtGeo<TR, TC>::kWarps, 16 / (TR * TC))
   __shared__ __align__(8) uint64_t bars[Gm::kWarps];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int n_twc = (a.nw + TC - 1) / TC, n_thr = (a.nh + TR - 1) / TR;
-  const long long seg = blockIdx.x;
+  const uint32_t seg = blockIdx.x;  // 32-bit decode, as in the input transform
   const int kg = blockIdx.y;
-  const int twc = (int)(seg % n_twc);
-  const long long band = seg / n_twc;
-  const int thr = (int)(band % n_thr);
-  const long long b = band / n_thr;
+  const int twc = (int)(seg % (uint32_t)n_twc);
+  const uint32_t band = seg / (uint32_t)n_twc;
+  const int thr = (int)(band % (uint32_t)n_thr);
+  const long long b = band / (uint32_t)n_thr;
   const int tr = warp / TC, tc = warp - (warp / TC) * TC;
   const int th = thr * TR + tr, tw = twc * TC + tc;
   const bool live = th < a.nh && tw < a.nw;

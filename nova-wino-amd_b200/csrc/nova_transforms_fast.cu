@@ -156,9 +156,11 @@ __device__ __forceinline__ void block_coords(const Args& a, long long& lrow, int
   twc = blockIdx.x % a.n_twc;
   cg = blockIdx.x / a.n_twc;
   lrow = a.lrow0 + blockIdx.y;
-  const long long grow = a.row0 + lrow;
-  b = (int)(grow / a.nh);
-  th = (int)(grow - (long long)b * a.nh);
+  // Tile rows (b * nh + th) stay below 2^31: 32-bit division, not the long
+  // emulated 64-bit one.
+  const uint32_t grow = (uint32_t)(a.row0 + lrow);
+  b = (int)(grow / (uint32_t)a.nh);
+  th = (int)(grow - (uint32_t)b * (uint32_t)a.nh);
 }
 
 template <int TPC, int G>
@@ -505,11 +507,12 @@ __global__ void __launch_bounds__(32 * StreamGeo<TPC>::kWarps, 1)
         const int sl = (int)(j % Sg::kSlots);
         const uint32_t ph = (uint32_t)((j / Sg::kSlots) & 1);
         if (!mbar_wait_bounded(tc::smem_u32(&empty[sl]), ph ^ 1u)) break;
-        const long long lrow = item / per_row;
+        const long long lrow = (uint32_t)item / (uint32_t)per_row;  // items < 2^31
         const int bx = (int)(item - lrow * per_row);
         const int twc = bx % a.n_twc, cg = bx / a.n_twc;
         const long long grow = a.row0 + lrow;
-        const int b = (int)(grow / a.nh), th = (int)(grow - (long long)b * a.nh);
+        const int b = (int)((uint32_t)grow / (uint32_t)a.nh),
+                  th = (int)(grow - (long long)b * a.nh);
         const int w0 = twc * TPC * 6 - a.pad;
         const int x0 = w0 >= 0 ? (w0 & ~7) : -((-w0 + 7) & ~7);
         const uint32_t fb = tc::smem_u32(&full[sl]);
@@ -530,7 +533,7 @@ __global__ void __launch_bounds__(32 * StreamGeo<TPC>::kWarps, 1)
       if ((int)(j % Sg::kGroups) != g) continue;
       const int sl = (int)(j % Sg::kSlots);
       const uint32_t ph = (uint32_t)((j / Sg::kSlots) & 1);
-      const long long lrow = item / per_row;
+      const long long lrow = (uint32_t)item / (uint32_t)per_row;  // items < 2^31
       const int bx = (int)(item - lrow * per_row);
       const int twc = bx % a.n_twc, cg = bx / a.n_twc;
       const int c0 = cg * Gm::kCGN;
