@@ -684,13 +684,27 @@ def config2_grid(device, flush, batches=(1, 8, 32, 128), reps=20):
                 ours_b2b = back_to_back_us(lambda: conv(x))
                 cud_b2b = back_to_back_us(lambda: F.conv2d(x, w16, padding=1))
                 y = conv(x)
+                # The same point channels-last: our NHWC kernels and cuDNN's
+                # channels-last convolution, graph-replayed after an L2 flush.
+                xl = x.contiguous(memory_format=torch.channels_last)
+                wl = w16.contiguous(memory_format=torch.channels_last)
+                for _ in range(3):
+                    F.conv2d(xl, wl, padding=1)
+                g_ours_l = graph_of(lambda: conv(xl))
+                g_cud_l = graph_of(lambda: F.conv2d(xl, wl, padding=1))
+                ours_l = time_kernel(g_ours_l.replay, reps, flush)
+                cud_l = time_kernel(g_cud_l.replay, reps, flush)
+                yl = conv(xl)
             fl = direct_flops(B, C, C, H)
             grid.setdefault(name, {})[str(B)] = {
                 "us": round(ours * 1e3, 2), "eff_tflops": round(fl / ours / 1e9, 1),
                 "cudnn_fp16_us": round(cud * 1e3, 2),
                 "us_b2b": round(ours_b2b, 2), "cudnn_fp16_us_b2b": round(cud_b2b, 2),
-                "parity": sample_parity(name, x, conv.weight, y)}
-            del x, y, g_ours, g_cud
+                "parity": sample_parity(name, x, conv.weight, y),
+                "nhwc_us": round(ours_l * 1e3, 2), "nhwc_eff_tflops": round(fl / ours_l / 1e9, 1),
+                "cudnn_fp16_channels_last_us": round(cud_l * 1e3, 2),
+                "nhwc_parity_ok": sample_parity(name, x, conv.weight, yl.contiguous())["ok"]}
+            del x, y, xl, yl, g_ours, g_cud, g_ours_l, g_cud_l
     return grid
 
 
@@ -1047,6 +1061,15 @@ def resnet50_measure(batch, steps, warmup, device, dist, world, rank):
         "logits_rel_diff_vs_nchw": float(((out_cl.float() - out.float()).norm() /
                                           out.float().norm()).item()),
     }
+    if rank == 0:
+        # Batch 1 channels-last, whole network captured in a CUDA graph.
+        x1 = x[:1].contiguous(memory_format=torch.channels_last)
+        for label, m in (("nova", model), ("cudnn", ref)):
+            with torch.no_grad():
+                g = graph_of(lambda: m(x1))
+                rec["channels_last"][f"batch1_{label}_graph_ms"] = round(
+                    back_to_back_us(g.replay, reps=50) / 1e3, 4)
+                del g
     del model, ref, x
     torch.cuda.empty_cache()
     return rec
