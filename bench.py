@@ -306,14 +306,18 @@ def time_kernel(fn, reps, flush):
     return statistics.mean(s.elapsed_time(e) for s, e in evs)
 
 
-def stage_profile(layers, batch, flush, reps=20):
+def stage_profile(layers, batch, flush, reps=20, nhwc=False):
     """Per-stage device times through the stage C-ABI entries (one launch each,
-    whole batch), with the algorithmic bytes / FLOPs of each launch."""
+    whole batch), with the algorithmic bytes / FLOPs of each launch.  nhwc:
+    the channels-last stage entries on the channels-last copies of the inputs
+    (the same bytes: x and y hold the same elements in either layout)."""
     import torch
     from nova_winograd import ops
     lib = ops.get_lib()
     out = []
     for name, C, H, conv, x in layers:
+        if nhwc:
+            x = x.contiguous(memory_format=torch.channels_last)
         nt = live_tiles(H)
         BP = batch * nt * nt
         V = torch.empty(64, BP, C, dtype=torch.float16, device=x.device)
@@ -323,25 +327,31 @@ def stage_profile(layers, batch, flush, reps=20):
         h = conv._handle
         s = ops.stream_ptr()
 
+        it_fn = lib.nova_input_transform_nhwc_v2 if nhwc else lib.nova_input_transform_v2
+        ot_fn = lib.nova_output_transform_nhwc_v2 if nhwc else lib.nova_output_transform_v2
+        if nhwc:
+            y = y.contiguous(memory_format=torch.channels_last)
+
         def it():
-            ops.check(lib.nova_input_transform_v2(ops.ptr(x), ops.ptr(V), batch, C, H, H, 1,
-                                                  nt, nt, BP, s), "input_transform")
+            ops.check(it_fn(ops.ptr(x), ops.ptr(V), batch, C, H, H, 1, nt, nt, BP, s),
+                      "input_transform")
 
         def gm():
             ops.check(lib.nova_batched_gemm_v2(h, ops.ptr(V), ops.ptr(M), BP, s), "gemm")
 
         def ot():
-            ops.check(lib.nova_output_transform_v2(ops.ptr(M), ops.ptr(y), batch, C, H, H,
-                                                   nt, nt, BP, s), "output_transform")
+            ops.check(ot_fn(ops.ptr(M), ops.ptr(y), batch, C, H, H, nt, nt, BP, s),
+                      "output_transform")
 
         x_b = y_b = batch * C * H * H * 2
         v_b = m_b = 64 * BP * C * 2
         u_b = 64 * C * C * 2
         gflop = 2.0 * 64 * C * C * BP
+        sfx = "_nhwc" if nhwc else ""
         for kname, fn, nbytes, flops in (
-                ("input_transform_kernel", it, x_b + v_b, 0.0),
+                ("input_transform_kernel" + sfx, it, x_b + v_b, 0.0),
                 ("gemm_tc_kernel", gm, v_b + u_b + m_b, gflop),
-                ("output_transform_kernel", ot, m_b + y_b, 0.0)):
+                ("output_transform_kernel" + sfx, ot, m_b + y_b, 0.0)):
             ms = time_kernel(fn, reps, flush)
             out.append({"layer": name, "kernel": kname, "ms": ms, "bytes": nbytes,
                         "flops": flops, "gbs": nbytes / ms / 1e6,
@@ -851,10 +861,15 @@ def run_nova(args):
             parity = {name: sample_parity(name, x, conv.weight, conv(x))
                       for name, C, H, conv, x in layers}
 
-    stages = roofline = lat = cpu = vendor = grid = b256 = None
+    stages = roofline = lat = cpu = vendor = grid = b256 = stages_nhwc = None
     if rank == 0:
         stages = stage_profile(layers, batch, flush)
         roofline = roofline_from_stages(stages, peaks, batch)
+        stages_nhwc = [
+            {"layer": st["layer"], "kernel": st["kernel"], "ms": round(st["ms"], 5),
+             "bytes": st["bytes"], "gbs": round(st["gbs"], 1),
+             "frac_of_hbm": round(st["gbs"] / peaks["hbm_gbs"], 3)}
+            for st in stage_profile(layers, batch, flush, nhwc=True) if "nhwc" in st["kernel"]]
         lat = b1_latency(device)
         vendor = vendor_layer_times(layers, flush, channels_last=True)
         if not args.quick:
@@ -895,6 +910,7 @@ def run_nova(args):
             "stages": [{k: (round(v, 5) if isinstance(v, float) else v) for k, v in st.items()}
                        for st in stages],
             "parity": parity,
+            "stages_nhwc": stages_nhwc,
             "b1_latency_us": lat,
             "per_layer_vs_cudnn": vendor,
             "config2_grid": grid,
