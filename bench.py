@@ -217,9 +217,11 @@ class ClockSampler:
         smax = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
         reasons = sorted({names[i] for r in rows for i in range(4) if r[3 + i] == "Active"})
+        pw = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
         return {"sm_mhz": statistics.median(sm) if sm else None,
                 "sm_max_mhz": max(smax) if smax else None, "reasons": reasons,
-                "samples": len(rows)}
+                "samples": len(rows),
+                "power_w_median": statistics.median(pw) if pw else None}
 
 
 def setup_dist():
@@ -718,6 +720,39 @@ def config2_grid(device, flush, batches=(1, 8, 32, 128), reps=20):
     return grid
 
 
+def gemm_sustained(gm, flops, device, peaks, seconds=1.5, per_graph=25):
+    """The GEMM back to back for about `seconds` (CUDA graphs of `per_graph`
+    launches, after half a second of the same load), with the SM clock and power
+    sampled meanwhile: the sustained rate, against the sustained peak."""
+    import torch
+    g = graph_of(lambda: [gm() for _ in range(per_graph)])
+    g.replay()
+    torch.cuda.synchronize()
+    t0 = time.time()
+    g.replay()
+    torch.cuda.synchronize()
+    n = max(10, int(seconds / max(time.time() - t0, 1e-4)))
+    uuid = str(torch.cuda.get_device_properties(device).uuid)
+    sampler = ClockSampler(uuid if uuid.startswith("GPU-") else f"GPU-{uuid}")
+    sampler.start()
+    for _ in range(n // 3):
+        g.replay()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    for _ in range(n):
+        g.replay()
+    e.record()
+    torch.cuda.synchronize()
+    clocks = sampler.stop()
+    ms = s.elapsed_time(e) / (n * per_graph)
+    tf = flops / ms / 1e9
+    del g
+    return {"launches": n * per_graph, "gemm_us": round(ms * 1e3, 2), "tflops": round(tf, 1),
+            "frac_of_sustained_peak": round(tf / peaks["bf16_tflops_sustained"], 4),
+            "sustained_peak": peaks["bf16_tflops_sustained"], "clocks": clocks,
+            "l2": "warm (operands partly L2-resident back to back)"}
+
+
 def gemm_stage_b256(device, flush, peaks, reps=20):
     """The north star's batch-256 GEMM stage: the tcgen05 GEMM alone (stage
     entry nova_batched_gemm_v2, L2 flushed) at batch 256 for conv2_x, conv4_x
@@ -753,7 +788,13 @@ def gemm_stage_b256(device, flush, peaks, reps=20):
         Mc = torch.empty_like(M)
         ms_cb = time_kernel(lambda: torch.bmm(V, Ut, out=Mc), reps, flush)
         del Ut, Mc
+        def gm_cur():  # on the current stream at call time (capturable)
+            ops.check(lib.nova_batched_gemm_v2(h, ops.ptr(V), ops.ptr(M), BP, ops.stream_ptr()),
+                      "gemm")
+
+        sustained = gemm_sustained(gm_cur, flops, device, peaks) if C == 512 else None
         out[name] = {"gemm_us": round(ms * 1e3, 2), "tflops": round(tf, 1),
+                     "sustained_loop": sustained,
                      "cublas_bmm_us": round(ms_cb * 1e3, 2),
                      "cublas_bmm_tflops": round(flops / ms_cb / 1e9, 1),
                      "frac_of_peak": round(tf / peaks["bf16_tflops"], 4),
