@@ -79,3 +79,23 @@ def test_forward_without_gpu_fails_loudly():
         conv(torch.zeros(1, 8, 8, 8, dtype=torch.float16))
     with pytest.raises(RuntimeError, match="CUDA device"):
         nova_winograd.compute_tiling(56, 56, 1)
+
+
+def test_nhwc_eligibility_rule():
+    """Channels-last inputs take the NHWC kernels only when C % 8 == 0, K is
+    even and the base is 16-byte aligned; plain-contiguous tensors (including
+    those that are both, C == 1 or H == W == 1) keep the NCHW path."""
+    import torch
+    from nova_winograd.ops import nhwc_eligible
+    cl = torch.channels_last
+    x = torch.zeros(2, 16, 9, 9, dtype=torch.float16).contiguous(memory_format=cl)
+    assert nhwc_eligible(x, 16)
+    assert not nhwc_eligible(x, 15)                       # odd K
+    assert not nhwc_eligible(torch.zeros(2, 12, 9, 9, dtype=torch.float16)
+                             .contiguous(memory_format=cl), 16)  # C % 8 != 0
+    assert not nhwc_eligible(torch.zeros(2, 16, 9, 9, dtype=torch.float16), 16)  # NCHW
+    both = torch.zeros(2, 16, 1, 1, dtype=torch.float16)  # contiguous in both formats
+    assert not nhwc_eligible(both, 16)
+    base = torch.zeros(2 * 16 * 9 * 9 + 1, dtype=torch.float16)
+    off = base[1:].view(2, 9, 9, 16).permute(0, 3, 1, 2)  # channels-last view, 2-byte offset
+    assert off.is_contiguous(memory_format=cl) and not nhwc_eligible(off, 16)
