@@ -6,25 +6,27 @@
 // window of a tile is 64 cells of C contiguous channels: a warp reads one cell
 // of 64 channels as one 128-byte line, so neither kernel needs the
 // shared-memory transposes of the NCHW kernels.  V and M keep the NCHW path's
-// layout ([pos][bp][channel]), so the tcgen05 GEMM between them is the same,
-// and every value of V, M and y is computed by the same operations in the
-// same order as on the NCHW path: the two layouts give the same values (a
-// term dropped for a known-zero input can only change the sign of an exact
-// zero).
+// layout ([pos][bp][channel]), so the tcgen05 GEMM between them is the same.
+// The butterflies are the NCHW plane kernels' (the same operations in the
+// same order); the NCHW row and streaming kernels order some FP32 sums
+// differently, so the two layouts agree within FP32 reordering.
 //
-// Both kernels: one warp per (tile, 64-channel group), lane = channel pair,
-// 4 warps per block.  The input transform lands each block's windows by one
-// TMA box load (C % 8 == 0); the output transform reads M and writes y with
-// plain 4-byte accesses (K even).
+// Both transforms: one warp per (tile, 64-channel group), lane = channel
+// pair; a block is TR x TC tiles of one image and one channel group.  The
+// input transform lands the block's window by one TMA box load (C % 8 == 0,
+// zeros outside the image from the tensor map).  The output transform lands
+// each tile's M by a TMA tile load and stores the block's outputs by one TMA
+// tile store (K % 8 == 0); for other even K a plain form reads M and writes y
+// with 4-byte accesses, 4 warps per block.
 #include "nova_common.cuh"
 #include "nova_internal.h"
 
 namespace nova {
 namespace nhwc {
 
-constexpr int kWarps = 4;
+constexpr int kWarps = 4;  // plain output transform: warps per block
 #ifndef NOVA_NHWC_OT_MIN_BLOCKS
-#define NOVA_NHWC_OT_MIN_BLOCKS 3  // output transform: 168 registers (8 bytes spill at 128)
+#define NOVA_NHWC_OT_MIN_BLOCKS 3  // plain output transform: 168 registers (8 bytes spill at 128)
 #endif
 constexpr int kMinBlocks = NOVA_NHWC_OT_MIN_BLOCKS;
 
