@@ -467,7 +467,7 @@ def roofline_from_stages(stages, peaks, batch=128):
     return rl
 
 
-def b1_latency(device, reps=200):
+def b1_latency(device, reps=200, nhwc=True):
     """Per-layer batch-1 latency (us): back-to-back module calls (host overhead
     included) and the same call replayed from a CUDA graph (device only); the
     same for the channels-last input (the NHWC kernels) under "nhwc"."""
@@ -475,8 +475,9 @@ def b1_latency(device, reps=200):
     res = {}
     for name, C, H, conv, x in build_layers(1, device):
         res[name] = _b1_one(conv, x, C, H, reps)
-        res[name]["nhwc"] = _b1_one(conv, x.contiguous(memory_format=torch.channels_last), C, H,
-                                    reps)
+        if nhwc:
+            res[name]["nhwc"] = _b1_one(conv, x.contiguous(memory_format=torch.channels_last), C,
+                                        H, reps)
     return res
 
 
@@ -906,13 +907,14 @@ def run_nova(args):
     if rank == 0:
         stages = stage_profile(layers, batch, flush)
         roofline = roofline_from_stages(stages, peaks, batch)
-        stages_nhwc = [
-            {"layer": st["layer"], "kernel": st["kernel"], "ms": round(st["ms"], 5),
-             "bytes": st["bytes"], "gbs": round(st["gbs"], 1),
-             "frac_of_hbm": round(st["gbs"] / peaks["hbm_gbs"], 3)}
-            for st in stage_profile(layers, batch, flush, nhwc=True) if "nhwc" in st["kernel"]]
-        lat = b1_latency(device)
-        vendor = vendor_layer_times(layers, flush, channels_last=True)
+        if not args.quick:
+            stages_nhwc = [
+                {"layer": st["layer"], "kernel": st["kernel"], "ms": round(st["ms"], 5),
+                 "bytes": st["bytes"], "gbs": round(st["gbs"], 1),
+                 "frac_of_hbm": round(st["gbs"] / peaks["hbm_gbs"], 3)}
+                for st in stage_profile(layers, batch, flush, nhwc=True) if "nhwc" in st["kernel"]]
+        lat = b1_latency(device, nhwc=not args.quick)
+        vendor = vendor_layer_times(layers, flush, channels_last=not args.quick)
         if not args.quick:
             grid = config2_grid(device, flush)
             b256 = gemm_stage_b256(device, flush, peaks)
@@ -1443,8 +1445,8 @@ def main():
     ap.add_argument("--impl", choices=["nova", "reference"], default="nova")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--quick", action="store_true",
-                    help="sweep only: skip the batch 1/8/32 grid, the batch-256 GEMM stage and "
-                         "the ResNet-50 record")
+                    help="sweep only: skip the batch 1/8/32 grid, the batch-256 GEMM stage, the "
+                         "ResNet-50 record and the channels-last records")
     ap.add_argument("--workload",
                     choices=["sweep", "resnet50", "sd15", "sdxl", "sd15_layers", "sdxl_layers"],
                     default="sweep",
