@@ -1161,6 +1161,7 @@ def run_resnet50(args):
             "logits_rel_diff_vs_cudnn": rec["logits_rel_diff_vs_cudnn"],
             "conv_parity_image0": rec.get("conv_parity_image0"),
             "batch1": rec.get("batch1"),
+            "channels_last": rec.get("channels_last"),
             "clocks": clocks,
         })
     if dist is not None:
