@@ -84,6 +84,20 @@ def test_null_handle_and_argument_errors(lib):
     assert lib.nova_get_last_error(None) == 1
 
 
+def test_nhwc_entries_validate_before_any_launch(lib):
+    fake = ctypes.c_void_p(0x1000)
+    # Null tensors, C % 8 != 0, odd K, misaligned x, BP short of the tiling.
+    assert lib.nova_forward_nhwc_v2(None, None, None, 1, 8, 8, 1, None) == 1
+    assert lib.nova_input_transform_nhwc_v2(None, None, 1, 8, 8, 8, 1, 2, 2, 4, None) == 1
+    assert lib.nova_input_transform_nhwc_v2(fake, fake, 1, 12, 8, 8, 1, 2, 2, 4, None) == 1
+    assert lib.nova_input_transform_nhwc_v2(ctypes.c_void_p(0x1004), fake, 1, 8, 8, 8, 1, 2, 2,
+                                            4, None) == 1
+    assert lib.nova_input_transform_nhwc_v2(fake, fake, 2, 8, 8, 8, 1, 2, 2, 7, None) == 1
+    assert lib.nova_output_transform_nhwc_v2(fake, fake, 1, 7, 8, 8, 2, 2, 4, None) == 1
+    assert lib.nova_output_transform_nhwc_v2(None, fake, 1, 8, 8, 8, 2, 2, 4, None) == 1
+    assert b"bad arguments" in lib.nova_last_error_string()
+
+
 def test_stage_bp_smaller_than_tiling_rejected(lib):
     fake = ctypes.c_void_p(0x1000)
     # BP must cover batch*nh*nw.
