@@ -1293,8 +1293,8 @@ def gemm_trace(args):
     warpgroups for a finished accumulator and for their slab's previous TMA
     store; and the CTA's whole time.  Printed as microseconds at the clock
     given by --trace-mhz, averaged over the CTAs and --steps launches, for
-    conv4_x and conv5_x at batch 128 and 256, L2 flushed before each launch
-    and warm."""
+    every sweep layer at batch 128 and conv2_x, conv4_x and conv5_x at batch
+    256, L2 flushed before each launch and warm."""
     import ctypes
     import numpy as np
     import torch
@@ -1319,8 +1319,9 @@ def gemm_trace(args):
     if os.environ.get("NOVA_GEMM_PAIR") == "1":
         nsm -= nsm % 2  # one CTA per SM of the pairs
     out = {"unit": f"us at {args.trace_mhz} MHz (SM-clock cycles / MHz)"}
-    for B in (128, 256):
-        shapes = [l for l in LAYERS if l[0] in ("conv4_x", "conv5_x")]
+    for B, names in ((128, ("conv2_x", "conv3_x", "conv4_x", "conv5_x")),
+                     (256, ("conv2_x", "conv4_x", "conv5_x"))):
+        shapes = [l for l in LAYERS if l[0] in names]
         for name, C, H, conv, x in build_layers(B, device, shapes):
             nt = live_tiles(H)
             BP = B * nt * nt
